@@ -1,0 +1,178 @@
+/*
+ * clef_b200.h -- C ABI of libclef_b200.so, the B200 (sm_100a) implementation of
+ * deciax's Clef prefill-and-score path.
+ *
+ * The library replaces the device side of `ClefModel` in the reference
+ * (src/deciax/models/clef/model.py:30-102): weight placement
+ * (models/clef/weights.py:70-101), the per-layer forward (models/qwen3_5/text.py:94-102
+ * and its Pallas TP form models/qwen3_5/pallas.py:132-150), the final norm,
+ * the lexical option means and the joint schema head (models/clef/head.py:50-107).
+ * Host code keeps tokenisation, collate and decode (models/clef/input.py).
+ *
+ * Conventions
+ *  - Every function returns 0 on success or a CLEF_E* status; clef_last_error()
+ *    gives a message.  CLEF_EINVAL marks bad shapes/config/names (the reference
+ *    raises ValueError there -> HTTP 422); CLEF_ECUDA / CLEF_ENCCL / CLEF_EDEVICE
+ *    mark device failures (RuntimeError -> HTTP 500).
+ *  - Plain pointers and sizes only.  Host buffers are caller-owned.
+ *  - One handle drives one GPU (one tensor-parallel rank).  Calls on one handle
+ *    must be serialised by the caller (the reference's ClefEngine holds a lock,
+ *    runtime/clef.py:21,36); distinct handles are independent.
+ */
+#ifndef CLEF_B200_H
+#define CLEF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CLEF_OK 0
+#define CLEF_EINVAL 1   /* bad argument, shape, name or configuration */
+#define CLEF_ECUDA 2    /* CUDA runtime error */
+#define CLEF_ENCCL 3    /* NCCL error */
+#define CLEF_EDEVICE 4  /* a kernel reported a device-side status (timeout, bad index) */
+#define CLEF_ESTATE 5   /* call out of order (e.g. forward before finalize) */
+
+#define CLEF_DTYPE_F32 0
+#define CLEF_DTYPE_BF16 1
+
+#define CLEF_LAYER_FULL_ATTENTION 0
+#define CLEF_LAYER_LINEAR_ATTENTION 1
+
+/* Model configuration: the reference TextConfig (models/qwen3_5/config.py:10-75)
+ * plus joint_head_config.json (models/clef/model.py:80-83).  The three
+ * beyond-reference fields default to 0 = off = reference semantics. */
+typedef struct ClefConfig {
+  int32_t hidden_size;           /* D */
+  int32_t intermediate_size;     /* F */
+  int32_t num_attention_heads;   /* Hq */
+  int32_t num_key_value_heads;   /* Hkv */
+  int32_t head_dim;              /* d */
+  int32_t num_layers;
+  const int32_t* layer_types;    /* [num_layers] CLEF_LAYER_*; NULL = all full attention */
+  int32_t vocab_size;
+  float rms_norm_eps;
+  float rope_theta;
+  float partial_rotary_factor;
+  int32_t max_seq_len;           /* longest sequence a forward may use (RoPE table) */
+  /* joint schema head */
+  int32_t head_width;            /* W */
+  int32_t head_heads;
+  int32_t head_routing_layers;
+  int32_t head_layers;
+  int32_t head_ffn;              /* rows of feedforward.0 / linear1 */
+  /* beyond-reference options (not in deciax; 0 = off) */
+  float attn_softcap;            /* softcap * tanh(score / softcap) on attention scores */
+  const int32_t* layer_window;   /* [num_layers] causal window per layer, 0 = global; NULL = all global */
+  float embed_scale;             /* multiply embeddings by this in the activation dtype */
+} ClefConfig;
+
+/* One collated batch: the dict returned by the reference collate()
+ * (models/clef/input.py:140-182).  Shapes: b rows, s sequence bucket,
+ * lx lexical length, o option bucket, q question bucket. */
+typedef struct ClefBatch {
+  int32_t b, s, lx, o, q;
+  const int32_t* input_ids;       /* [b, s] */
+  const uint8_t* mask;            /* [b, s] 0/1 */
+  const int32_t* lexical_ids;     /* [b, lx] */
+  const int32_t* lexical_spans;   /* [b, o, 2] */
+  const int32_t* question_spans;  /* [b, q, 2] */
+  const uint8_t* question_mask;   /* [b, q] */
+  const int32_t* types;           /* [b, q] */
+  const int32_t* option_spans;    /* [b, o, 2] */
+  const uint8_t* option_mask;     /* [b, o] */
+  const int32_t* option_field;    /* [b, o] */
+} ClefBatch;
+
+/* ---- model lifecycle: replaces ClefModel.__init__ (models/clef/model.py:34-85) ---- */
+
+/* Size of an NCCL unique id; rank 0 makes one, every rank passes the same bytes. */
+#define CLEF_NCCL_ID_BYTES 128
+int clef_nccl_unique_id(uint8_t out[CLEF_NCCL_ID_BYTES]);
+
+/* Create a model on `device` as tensor-parallel rank tp_rank of tp_size
+ * (mesh of models/clef/model.py:59-63; heads and MLP columns sharded as
+ * models/clef/weights.py:60-67).  nccl_id may be NULL when tp_size == 1.
+ * dtype: CLEF_DTYPE_BF16 (serving) or CLEF_DTYPE_F32 (parity). */
+int clef_create(const ClefConfig* config, int device, int tp_rank, int tp_size, const uint8_t* nccl_id, int dtype,
+                void** handle);
+
+/* Upload one tensor from host memory (models/clef/weights.py:70-101).  The
+ * library converts to the compute dtype, keeps this rank's shard and packs it.
+ * Names: "embedding", "lm_head", "norm",
+ *   "layers.{i}.{input_layernorm,post_attention_layernorm}.weight",
+ *   "layers.{i}.mixer.{q_proj,k_proj,v_proj,o_proj,q_norm,k_norm}.weight",
+ *   "layers.{i}.mlp.{gate_proj,up_proj,down_proj}.weight",
+ *   "head.<joint_head.safetensors key>".
+ * host_dtype: CLEF_DTYPE_F32 or CLEF_DTYPE_BF16 (raw bfloat16 bits). */
+int clef_upload(void* handle, const char* name, const void* host, int host_dtype, const int64_t* shape, int ndim);
+
+/* Check every tensor is present and build the packed layouts. */
+int clef_finalize(void* handle);
+
+/* ClefModel.forward (models/clef/model.py:92-102): host batch in, option
+ * logits [b, o] float32 out (host).  out_hidden, if not NULL, receives the
+ * final-normed hidden states [b, s, hidden] as float32.  All ranks of a TP
+ * group must call it with the same batch. */
+int clef_forward(void* handle, const ClefBatch* batch, float* out_logits, float* out_hidden);
+
+/* Lexical means + joint head only (models/clef/model.py:100-102,
+ * models/clef/head.py:50-107) on caller-supplied final-normed hidden states
+ * [b, s, hidden] float32 (host) -- the input of the reference's joint-head
+ * fixture test (tests/clef/test_head.py:11-29). */
+int clef_forward_head(void* handle, const ClefBatch* batch, const float* hidden, float* out_logits);
+
+/* Same computation with every ClefBatch pointer and out_logits in device
+ * memory of this handle's GPU, enqueued on `stream` (a cudaStream_t; NULL =
+ * the library's stream).  No host synchronisation and no allocation once the
+ * workspace for this shape exists (see clef_reserve). */
+int clef_forward_device(void* handle, const ClefBatch* batch, float* out_logits, void* stream);
+
+/* Allocate the workspace for batches up to (b, s, lx, o, q) ahead of time. */
+int clef_reserve(void* handle, int b, int s, int lx, int o, int q);
+
+/* Synchronise the device and report (then clear) any device-side status a
+ * kernel recorded since the last check (CLEF_EDEVICE: wait timeout or an
+ * out-of-range token id).  clef_forward does this itself. */
+int clef_check_status(void* handle);
+
+/* Number of kernels the last forward launched (for launch accounting). */
+int clef_last_launch_count(void* handle);
+
+int clef_destroy(void* handle);
+
+/* Message of the last failure on this handle (or of the last global failure when NULL). */
+const char* clef_last_error(void* handle);
+
+/* ---- kernel-level entry points (device pointers; used by the parity tests) ----
+ * All run on `stream` (cudaStream_t, NULL = default stream) on the current device
+ * and return CLEF_E* status after checking arguments. */
+
+/* C[M,N] = A[M,K] B[N,K]^T with a fused epilogue (nn.py:11-19, text.py:21-22):
+ * epi 0 store T(acc+bias) | 1 SwiGLU of packed [128 gate|128 up] blocks
+ * (kernels/swiglu.py:100-101) | 2 residual T(res + T(acc)) | 3 float acc.
+ * dtype BF16 runs the tcgen05 kernel, F32 the CUDA-core kernel. */
+int clef_op_gemm(int dtype, int epi, int M, int N, int K, const void* A, const void* B, void* out, int ldo,
+                 const void* bias, const void* residual, int ldr, void* stream);
+
+/* RMSNorm scaling by (1 + w) (models/qwen3_5/text.py:25-28). */
+int clef_op_rmsnorm(int dtype, const void* x, const void* w, void* out, int rows, int dim, float eps, void* stream);
+
+/* In-place per-head q/k RMSNorm + partial RoPE on a packed projection
+ * [b*s, Hq*2d + 2*Hkv*d] (models/qwen3_5/text.py:79-88, nn.py:31-44). */
+int clef_op_qk_norm_rope(int dtype, void* qkv, int b, int s, int hq, int hkv, int d, float partial_rotary_factor,
+                         float rope_theta, const void* q_norm, const void* k_norm, float eps, void* stream);
+
+/* Causal GQA attention with the sigmoid output gate over a packed projection
+ * (kernels/attention/blocked.py:9-32, text.py:90-91): out [b*s, Hq*d]. */
+int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out, int b, int s, int hq, int hkv, int d,
+                      float softcap, int window, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CLEF_B200_H */
