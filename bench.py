@@ -1,0 +1,425 @@
+"""Clef prefill-and-score benchmark on B200 (the BASELINE ``configs[1]`` workload).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload ("cfg2"): a clef-flash-shaped model -- 42 full-attention Qwen3.5
+layers, hidden 3584, 16 query / 8 key-value heads of 256, gated-MLP 14336,
+vocab 256000, lm_head = a copy of the embedding -- in BF16 with random
+N(0, 0.02) weights (seed 1), and the joint schema head (width 256, 4 heads,
+2 routing + 2 field layers; its real dims are not published).  One step is
+one full forward of 8 states x 2048 tokens (uniform token ids) carrying 4
+choice questions x 4 options each, from token ids to option logits.
+
+Output: one JSON line.  ``value`` = prefill tokens/s with the batch already
+resident in HBM, timed with CUDA events on the launching stream over exactly
+K steps (max over ranks).  ``e2e`` = the same metric through the public host
+API (``ClefCudaModel.forward`` -> ``clef_forward``), which copies the collated
+host arrays in and the logits out every step.  ``roofline`` = the dominant
+kernel (the gate/up GEMM with the fused SwiGLU epilogue) timed live by CUDA
+events inside the timed region.  ``cpu_baseline`` = the CPU oracle (FP32,
+the reference's impl="auto" arithmetic) on a bounded sample, extrapolated.
+
+With torchrun (N > 1) every rank holds a full replica and runs its own batch
+(data parallel, no collective on the data path): ``scaling`` is "weak".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "prefill tokens/s and decisions/s, clef-flash/clef BF16, 1/2/4/8 B200"
+UNIT = "tokens/s"
+CFG2 = dict(hidden_size=3584, intermediate_size=14336, num_attention_heads=16, num_key_value_heads=8, head_dim=256,
+            num_layers=42, vocab_size=256000)
+HEAD = dict(heads=4, routing_layers=2, layers=2, width=256, ffn=512)
+STATES, SEQ, QUESTIONS, OPTIONS = 8, 2048, 4, 4
+WEIGHT_SEED, WEIGHT_STD = 1, 0.02
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {
+        "workload": "cfg2: clef-flash-shaped prefill+scoring, 42 full-attention layers (D3584, 16q/8kv x256, F14336, "
+        "V256000), joint head W256/4 heads/2+2 layers; 8 states x 2048 tokens, 4 choice x 4 options per state",
+        "model": "clef-flash-shaped, random init N(0,0.02) seed 1",
+        "global_batch": STATES * n_gpus,
+        "seq_len": SEQ,
+        "parallelism": f"dp{n_gpus}" if n_gpus > 1 else "single",
+        "l2": "inputs larger than L2: every step streams 21 GB of weights and >1 GB of activations",
+    }
+
+
+def algorithmic_flops(c, lengths) -> tuple[float, float, float]:
+    """(linear FLOPs, attention FLOPs, gate/up FLOPs) for one batch, real tokens only."""
+    D, F, hq, hkv, d, L = c["hidden_size"], c["intermediate_size"], c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"], c["num_layers"]
+    tokens = sum(lengths)
+    linear = 2.0 * D * (2 * hq * d + 2 * hkv * d + hq * d + 3 * F) * tokens * L
+    attention = sum(2.0 * hq * d * n * (n + 1) for n in lengths) * L
+    return linear, attention, 2.0 * D * 2 * F
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()) | {"source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.sw_power_cap",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown")
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        assert self.proc and self.proc.stdout
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc) -> None:
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != len(self.FIELDS):
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ("sw_power_cap", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown")
+        reasons = sorted({n for _, _, flags in rows for n, f in zip(names, flags) if f.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# model on the device
+# ---------------------------------------------------------------------------
+
+
+def build_model(device: int):
+    """cfg2 in BF16: backbone weights drawn on the GPU (torch RNG), head from NumPy."""
+    import torch
+
+    from deciax_b200.build import build as build_lib
+    from deciax_b200.config import HeadConfig, TextConfig
+    from deciax_b200.model import ClefCudaModel
+    from deciax_b200.synthetic import synthetic_head_weights
+
+    build_lib()
+    config = TextConfig.full_attention(**CFG2)
+    head = HeadConfig(**HEAD)
+    model = ClefCudaModel(config, head, dtype="bf16", device=device, max_seq_len=SEQ)
+    gen = torch.Generator(device=f"cuda:{device}")
+    gen.manual_seed(WEIGHT_SEED)
+    D, F, hq, hkv, d, V = (CFG2[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads", "head_dim", "vocab_size"))
+
+    def randn(*shape):
+        t = torch.empty(shape, dtype=torch.bfloat16, device=f"cuda:{device}")
+        return t.normal_(0.0, WEIGHT_STD, generator=gen)
+
+    emb = randn(V, D)
+    model.upload_device("embedding", emb)
+    model.upload_device("lm_head", emb)  # "tied" = the same array written twice
+    del emb
+    model.upload_device("norm", randn(D))
+    shapes = {
+        "input_layernorm.weight": (D,), "post_attention_layernorm.weight": (D,), "mixer.q_proj.weight": (hq * 2 * d, D),
+        "mixer.k_proj.weight": (hkv * d, D), "mixer.v_proj.weight": (hkv * d, D), "mixer.o_proj.weight": (D, hq * d),
+        "mixer.q_norm.weight": (d,), "mixer.k_norm.weight": (d,), "mlp.gate_proj.weight": (F, D),
+        "mlp.up_proj.weight": (F, D), "mlp.down_proj.weight": (D, F),
+    }
+    for i in range(CFG2["num_layers"]):
+        for name, shape in shapes.items():
+            model.upload_device(f"layers.{i}.{name}", randn(*shape))
+    for k, v in synthetic_head_weights(D, head, seed=WEIGHT_SEED, std=WEIGHT_STD, dtype="bf16").items():
+        model.upload("head." + k, v)
+    model.finalize()
+    torch.cuda.synchronize(device)
+    return model
+
+
+def make_batch(seed: int) -> dict[str, np.ndarray]:
+    from deciax_b200.synthetic import BatchSpec, synthetic_batch
+
+    return synthetic_batch(BatchSpec(states=STATES, seq=SEQ, questions=QUESTIONS, options_per_question=OPTIONS),
+                           CFG2["vocab_size"], seed)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (FP32) on a bounded sample
+# ---------------------------------------------------------------------------
+
+
+def cpu_sample(repeats: int = 1) -> dict:
+    """One decoder layer + the joint head for one 2048-token state, FP32 NumPy,
+    extrapolated to the 42-layer model: tokens/s = 2048 / (42 t_layer + t_head)."""
+    from deciax_b200.config import HeadConfig
+    from deciax_b200.synthetic import synthetic_head_weights
+    from oracle import clef_oracle as O
+
+    rng = np.random.default_rng(0)
+    D, F, hq, hkv, d = (CFG2[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads", "head_dim"))
+
+    def n(*shape):
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(WEIGHT_STD)
+
+    p = {"input_layernorm.weight": n(D), "post_attention_layernorm.weight": n(D), "mixer.q_proj.weight": n(hq * 2 * d, D),
+         "mixer.k_proj.weight": n(hkv * d, D), "mixer.v_proj.weight": n(hkv * d, D), "mixer.o_proj.weight": n(D, hq * d),
+         "mixer.q_norm.weight": n(d), "mixer.k_norm.weight": n(d), "mlp.gate_proj.weight": n(F, D),
+         "mlp.up_proj.weight": n(F, D), "mlp.down_proj.weight": n(D, F)}
+    c = O.TextConfig(hidden_size=D, intermediate_size=F, num_attention_heads=hq, num_key_value_heads=hkv, head_dim=d)
+    hp = synthetic_head_weights(D, HeadConfig(**HEAD), seed=1)
+    arrays = {k: v[:1] for k, v in make_batch(seed=0).items()}
+    x = rng.standard_normal((1, SEQ, D), dtype=np.float32)
+    lex = rng.standard_normal((1, arrays["option_mask"].shape[1], D), dtype=np.float32)
+    t_layer = t_head = 0.0
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        h = O.layer(p, x, arrays["mask"], c, linear_attention=False, dtype="fp32")
+        t1 = time.perf_counter()
+        O.head_forward(hp, h, lex, arrays, heads=HEAD["heads"], routing_layers=HEAD["routing_layers"], layers=HEAD["layers"], dtype="fp32")
+        t2 = time.perf_counter()
+        t_layer += t1 - t0
+        t_head += t2 - t1
+    t_layer /= repeats
+    t_head /= repeats
+    per_state = CFG2["num_layers"] * t_layer + t_head
+    return {"value": SEQ / per_state, "unit": UNIT, "cores": len(os.sched_getaffinity(0)), "kind": "port",
+            "sample": f"oracle FP32 NumPy: 1 decoder layer ({t_layer:.2f} s) + joint head ({t_head:.2f} s) on one "
+            f"2048-token state, extrapolated to 42 layers ({per_state:.1f} s per state); embedding gather excluded",
+            "seconds": t_layer + t_head}
+
+
+def reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_sample()
+    samples = [cpu_sample() for _ in range(args.steps)]
+    value = statistics.mean(s["value"] for s in samples)
+    cb = dict(samples[-1])
+    cb["value"] = value
+    cb.pop("seconds", None)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(s["seconds"] for s in samples),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": workload_config(args.gpus), "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference CPU path = the NumPy restatement of deciax's impl=\"auto\" Clef forward (JAX is not installed)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+
+def gpu_arm(args) -> None:
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    from deciax_b200 import _lib
+    from deciax_b200.synthetic import field_probabilities
+
+    model = build_model(local)
+    arrays = make_batch(seed=100 + rank)
+    tensors = {k: torch.from_numpy(np.ascontiguousarray(arrays[k]).astype(np.uint8 if arrays[k].dtype == bool else np.int32)).cuda()
+               for k in _lib.BATCH_KEYS}
+    out = torch.empty(arrays["option_mask"].shape, dtype=torch.float32, device="cuda")
+    # A real stream: the library enqueues on it and the CUDA events below are
+    # recorded on it.  (torch's default stream is the legacy NULL stream, for
+    # which the library would use its own stream instead.)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    # --- device-resident throughput ---
+    for _ in range(args.warmup):
+        model.forward_device(tensors, out, stream.cuda_stream)
+    torch.cuda.synchronize()
+    model.check_status()
+    barrier()
+    torch.cuda.synchronize()
+    model.set_timing(True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            model.forward_device(tensors, out, stream.cuda_stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(end)
+    timing = model.timing_report()
+    model.set_timing(False)
+    model.check_status()
+    launches = model.last_launch_count * args.steps
+    logits_dev = out.cpu().numpy()
+    if not np.isfinite(logits_dev[arrays["option_mask"]]).all():
+        raise SystemExit("non-finite logits")
+
+    # --- end to end through the host API ---
+    h2d = sum(int(np.asarray(arrays[k]).size * (1 if arrays[k].dtype == bool else 4)) for k in _lib.BATCH_KEYS)
+    d2h = int(np.asarray(arrays["option_mask"]).size * 4)
+    model.forward(arrays)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        logits = model.forward(arrays)
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    decisions = sum(len(f) for f in field_probabilities(logits, arrays))
+
+    def max_over_ranks(v: float) -> float:
+        if not dist:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    elapsed_ms = max_over_ranks(elapsed_ms)
+    e2e_s = max_over_ranks(e2e_s)
+    tokens = STATES * SEQ
+    value = world * tokens * args.steps / (elapsed_ms / 1e3)
+    e2e_value = world * tokens * args.steps / e2e_s
+    linear, attention, gu_flops_per_token = algorithmic_flops(CFG2, [SEQ] * STATES)
+    peaks = measured_peaks()
+    step_s = elapsed_ms / 1e3 / args.steps
+    gu_ms, gu_n = timing["gemm_gate_up"]
+    gu_avg_s = gu_ms / 1e3 / max(gu_n, 1)
+    gu_flops = gu_flops_per_token * tokens
+    achieved = gu_flops / gu_avg_s / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    total_ms = sum(ms for ms, _ in timing.values())
+    shares = {k: round(ms / total_ms, 4) for k, (ms, _) in timing.items() if ms > 0}
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights, uniform token ids)",
+        "config": workload_config(world),
+        "decisions_per_s": world * decisions * args.steps / (elapsed_ms / 1e3),
+        "tensor_frac": {"flops_per_step": linear + attention, "achieved_tflops": (linear + attention) / step_s / 1e12,
+                        "frac_of_measured_burst": (linear + attention) / step_s / 1e12 / peaks["bf16_tflops"],
+                        "frac_of_measured_sustained": (linear + attention) / step_s / 1e12 / peaks["bf16_tflops_sustained"],
+                        "peak_source": peaks["source"]},
+        "roofline": {"kernel": "gemm_gate_up (tcgen05, fused SwiGLU epilogue)", "bound": "tensor", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_kind": f"bf16_tflops_sustained of {peaks['source']} (kernel timed inside a long step)",
+                     "flops_per_launch": gu_flops, "avg_launch_ms": gu_avg_s * 1e3, "traffic": traffic_per_launch()},
+        "kernel_ms_per_step": {k: round(ms / args.steps, 3) for k, (ms, _) in timing.items() if ms > 0},
+        "timeline_ms_per_step": total_ms / args.steps,  # cross-check of ms_per_step from the per-launch events
+        "kernel_share": shares,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_sample(repeats=4)
+        cb.pop("seconds", None)
+        line["cpu_baseline"] = cb
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def traffic_per_launch():
+    """DRAM bytes per gate/up launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "gemm_gate_up_cfg2.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_full_launch:"):
+            return float(line.split(":", 1)[1].split()[0])
+    return None
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -21,12 +21,15 @@ EXPORTS = (
     "clef_nccl_unique_id",
     "clef_create",
     "clef_upload",
+    "clef_upload_device",
     "clef_finalize",
     "clef_forward",
     "clef_forward_head",
     "clef_forward_device",
     "clef_reserve",
     "clef_check_status",
+    "clef_set_timing",
+    "clef_timing_report",
     "clef_last_launch_count",
     "clef_destroy",
     "clef_last_error",
@@ -118,6 +121,9 @@ def load() -> ctypes.CDLL:
             "clef_nccl_unique_id": [ctypes.c_char_p],
             "clef_create": [ctypes.POINTER(ClefConfigC), i32, i32, i32, ctypes.c_char_p, i32, ctypes.POINTER(vp)],
             "clef_upload": [vp, ctypes.c_char_p, vp, i32, ctypes.POINTER(ctypes.c_int64), i32],
+            "clef_upload_device": [vp, ctypes.c_char_p, vp, i32, ctypes.POINTER(ctypes.c_int64), i32],
+            "clef_set_timing": [vp, i32],
+            "clef_timing_report": [vp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int)],
             "clef_finalize": [vp],
             "clef_forward": [vp, ctypes.POINTER(ClefBatchC), vp, vp],
             "clef_forward_head": [vp, ctypes.POINTER(ClefBatchC), vp, vp],

@@ -146,11 +146,59 @@ static CUtensorMap tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint
 // kernel launchers
 // ===========================================================================
 
+// Kernel categories for the per-kernel timing report (clef_timing_report).
+enum Category : int {
+  kCatEmbed = 0,
+  kCatNorm = 1,
+  kCatGemmQkv = 2,
+  kCatQkRope = 3,
+  kCatAttention = 4,
+  kCatGemmO = 5,
+  kCatGemmGateUp = 6,
+  kCatGemmDown = 7,
+  kCatAllReduce = 8,
+  kCatResidual = 9,
+  kCatHead = 10,
+  kCatOther = 11,
+  kNumCategories = 12,
+};
+
+// Optional CUDA-event timeline: one event after every launch on the stream,
+// so launch i's device time is the gap between event i-1 and event i.
+struct Timeline {
+  bool enabled = false;
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  std::vector<int> cats;
+  cudaEvent_t next() {
+    if (used == pool.size()) {
+      cudaEvent_t e;
+      CUDA_CHECK(cudaEventCreate(&e));
+      pool.push_back(e);
+    }
+    return pool[used++];
+  }
+  ~Timeline() {
+    for (auto e : pool) cudaEventDestroy(e);
+  }
+};
+
 struct Launcher {
   cudaStream_t stream = nullptr;
   int* status = nullptr;
-  int count = 0;
-  void tick() { ++count; }
+  int count = 0;        // kernels of this library launched
+  int cat = kCatOther;  // category of the next launch
+  Timeline* timeline = nullptr;
+  void mark(int c) {
+    if (timeline && timeline->enabled) {
+      CUDA_CHECK(cudaEventRecord(timeline->next(), stream));
+      timeline->cats.push_back(c);
+    }
+  }
+  void tick() {
+    ++count;
+    mark(cat);
+  }
 };
 
 template <int BN, int EPI>
@@ -400,7 +448,28 @@ struct Model {
   std::vector<Layer> layers;
   std::map<std::string, Tensor> head;
   Workspace ws;
+  Timeline timeline;
   int last_launches = 0;
+  bool src_on_device = false;  // clef_upload_device: the source pointer is device memory
+
+  // Sum each category's device time over the recorded timeline, then reset it.
+  void timing_report(int n, float* ms, int* launches) {
+    for (int i = 0; i < n; ++i) {
+      ms[i] = 0.f;
+      launches[i] = 0;
+    }
+    if (timeline.used > 0) CUDA_CHECK(cudaEventSynchronize(timeline.pool[timeline.used - 1]));
+    for (size_t i = 1; i < timeline.used; ++i) {
+      const int c = timeline.cats[i];
+      if (c < 0 || c >= n) continue;
+      float t = 0.f;
+      CUDA_CHECK(cudaEventElapsedTime(&t, timeline.pool[i - 1], timeline.pool[i]));
+      ms[c] += t;
+      launches[c] += 1;
+    }
+    timeline.used = 0;
+    timeline.cats.clear();
+  }
 
   ~Model() {
     if (comm) ncclCommDestroy(comm);
@@ -527,6 +596,13 @@ struct Model {
   // into device rows starting at dst_row of a [*, dst_ld] matrix, converting dtype.
   void put_block(const void* host, int host_dtype, int64_t cols, int64_t r0, int64_t nrows, int64_t c0, int64_t ncols,
                  void* dev, int64_t dst_row, int64_t dst_ld) {
+    if (src_on_device) {
+      REQUIRE(host_dtype == dtype, "a device-resident upload must already be in the compute dtype");
+      CUDA_CHECK(cudaMemcpy2D(static_cast<uint8_t*>(dev) + static_cast<size_t>(dst_row) * dst_ld * esz, dst_ld * esz,
+                              static_cast<const uint8_t*>(host) + (static_cast<size_t>(r0) * cols + c0) * esz, cols * esz,
+                              ncols * esz, nrows, cudaMemcpyDeviceToDevice));
+      return;
+    }
     const size_t hsz = host_dtype == CLEF_DTYPE_F32 ? 4 : 2;
     std::vector<uint8_t> tmp;
     std::vector<uint8_t> rowbuf;
@@ -579,6 +655,12 @@ struct Model {
       Tensor& t = head[name.substr(5)];
       t.shape.assign(shape, shape + ndim);
       const int64_t n = t.numel();
+      if (src_on_device) {
+        REQUIRE(host_dtype == dtype, "a device-resident upload must already be in the compute dtype");
+        t.buf.alloc(std::max<size_t>(static_cast<size_t>(n) * esz, 16));
+        CUDA_CHECK(cudaMemcpy(t.buf.p, host, static_cast<size_t>(n) * esz, cudaMemcpyDeviceToDevice));
+        return;
+      }
       std::vector<uint8_t> tmp;
       convert(host, host_dtype, static_cast<size_t>(n), tmp);
       t.buf.alloc(std::max<size_t>(tmp.size(), 16));
@@ -852,7 +934,8 @@ struct Model {
   template <typename T>
   void forward_impl(const DevBatch& bt, float* logits, cudaStream_t st) {
     REQUIRE(finalized, "clef_forward before clef_finalize");
-    Launcher Lc{st, status.as<int>(), 0};
+    Launcher Lc{st, status.as<int>(), 0, kCatOther, &timeline};
+    Lc.mark(-1);  // timeline start marker
     const int B = bt.b, S = bt.s;
     const int Tt = B * S;
     Workspace& w = ws;
@@ -869,13 +952,16 @@ struct Model {
       embed_kernel<T><<<(Tt + warps - 1) / warps, warps * 32, 0, st>>>(bt.ids, embedding.as<T>(), x, Tt, D, V,
                                                                       cfg.embed_scale, Lc.status);
       CUDA_CHECK(cudaGetLastError());
+      Lc.cat = kCatEmbed;
       Lc.tick();
     }
     // 2. decoder layers (text.py:94-102; TP: pallas.py:62-129)
     const int ldqkv = Nqkv;
     for (int li = 0; li < L; ++li) {
       Layer& l = layers[li];
+      Lc.cat = kCatNorm;
       rmsnorm<T>(Lc, x, D, l.w_in.as<T>(), hbuf, D, Tt, D, eps);
+      Lc.cat = kCatGemmQkv;
       if constexpr (sizeof(T) == 2)
         gemm_bf16(Lc, kEpiStore, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
       else
@@ -887,6 +973,7 @@ struct Model {
             qkv, ldqkv, Tt, S, Hq_l, Hkv_l, d, rot, l.q_norm.as<T>(), l.k_norm.as<T>(), rope_cos.as<float>(),
             rope_sin.as<float>(), eps);
         CUDA_CHECK(cudaGetLastError());
+        Lc.cat = kCatQkRope;
         Lc.tick();
       }
       {
@@ -917,10 +1004,14 @@ struct Model {
         a.softcap = cfg.attn_softcap;
         a.window = layer_window[li];
         a.status = Lc.status;
+        Lc.cat = kCatAttention;
         attention<T>(Lc, a);
       }
+      Lc.cat = kCatGemmO;
       project_residual<T>(Lc, attn_out, Hq_l * d, l.w_o.as<T>(), x, Tt);
+      Lc.cat = kCatNorm;
       rmsnorm<T>(Lc, x, D, l.w_post.as<T>(), hbuf, D, Tt, D, eps);
+      Lc.cat = kCatGemmGateUp;
       if constexpr (sizeof(T) == 2) {
         gemm_bf16(Lc, kEpiSwiglu, hbuf, D, l.w_gu.as<bf16>(), D, Tt, 2 * Fp, D, act, Fp, nullptr, nullptr, 0);
       } else {
@@ -930,11 +1021,14 @@ struct Model {
         CUDA_CHECK(cudaGetLastError());
         Lc.tick();
       }
+      Lc.cat = kCatGemmDown;
       project_residual<T>(Lc, act, Fp, l.w_down.as<T>(), x, Tt);
     }
     // 3. final norm (model.py:99) -> hbuf
+    Lc.cat = kCatNorm;
     rmsnorm<T>(Lc, x, D, final_norm.as<T>(), hbuf, D, Tt, D, eps);
     // 4-5. lexical means and the joint head
+    Lc.cat = kCatHead;
     scoring<T>(Lc, bt, logits);
     last_launches = Lc.count;
   }
@@ -960,7 +1054,7 @@ struct Model {
     CUDA_CHECK(cudaMemcpyAsync(ws.h.p, tmp.data(), tmp.size(), cudaMemcpyHostToDevice, stream));
     const size_t nlog = static_cast<size_t>(b.b) * b.o;
     float* dlog = ws.f32small.as<float>() + nlog * 2;
-    Launcher Lc{stream, status.as<int>(), 0};
+    Launcher Lc{stream, status.as<int>(), 0, kCatHead, &timeline};
     if (dtype == CLEF_DTYPE_BF16)
       scoring<bf16>(Lc, d, dlog);
     else
@@ -989,11 +1083,15 @@ struct Model {
     else
       gemm_simt<T>(Lc, kSimtF32, in, K, w, K, Tt, D, K, part, D, nullptr, nullptr, 0);
     NCCL_CHECK(ncclAllReduce(part, part, static_cast<size_t>(Tt) * D, ncclFloat32, ncclSum, comm, Lc.stream));
+    Lc.mark(kCatAllReduce);
     const long long n = static_cast<long long>(Tt) * D;
     residual_add_f32_kernel<T><<<static_cast<int>(std::min<long long>((n + 255) / 256, 8192)), 256, 0, Lc.stream>>>(
         x, part, n);
     CUDA_CHECK(cudaGetLastError());
+    const int saved = Lc.cat;
+    Lc.cat = kCatResidual;
     Lc.tick();
+    Lc.cat = saved;
   }
 
   template <typename T>
@@ -1319,6 +1417,41 @@ int clef_upload(void* handle, const char* name, const void* host, int host_dtype
   return guarded(m, [&] {
     REQUIRE(m && name && (ndim == 0 || shape) && ndim >= 0 && ndim <= 4, "bad clef_upload arguments");
     m->upload(name, host, host_dtype, shape, ndim);
+  });
+}
+
+int clef_upload_device(void* handle, const char* name, const void* device_ptr, int dtype, const int64_t* shape,
+                       int ndim) {
+  Model* m = static_cast<Model*>(handle);
+  return guarded(m, [&] {
+    REQUIRE(m && name && (ndim == 0 || shape) && ndim >= 0 && ndim <= 4, "bad clef_upload_device arguments");
+    m->src_on_device = true;
+    try {
+      m->upload(name, device_ptr, dtype, shape, ndim);
+    } catch (...) {
+      m->src_on_device = false;
+      throw;
+    }
+    m->src_on_device = false;
+  });
+}
+
+int clef_set_timing(void* handle, int enable) {
+  Model* m = static_cast<Model*>(handle);
+  return guarded(m, [&] {
+    REQUIRE(m, "null handle");
+    m->timeline.enabled = enable != 0;
+    m->timeline.used = 0;
+    m->timeline.cats.clear();
+  });
+}
+
+int clef_timing_report(void* handle, int n, float* ms, int* launches) {
+  Model* m = static_cast<Model*>(handle);
+  return guarded(m, [&] {
+    REQUIRE(m && ms && launches && n > 0, "bad clef_timing_report arguments");
+    CUDA_CHECK(cudaSetDevice(m->device));
+    m->timing_report(n, ms, launches);
   });
 }
 

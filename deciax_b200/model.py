@@ -135,8 +135,33 @@ class ClefCudaModel:
         shape = (ctypes.c_int64 * max(a.ndim, 1))(*a.shape)
         _lib.check(self._lib.clef_upload(self._handle, name.encode(), a.ctypes.data, dt, shape, a.ndim), self._handle)
 
+    def upload_device(self, name: str, tensor: Any) -> None:
+        """Upload from a CUDA tensor on this model's GPU, already in the compute dtype."""
+        import torch
+
+        want = torch.bfloat16 if self.dtype == "bf16" else torch.float32
+        if tensor.dtype != want or not tensor.is_cuda or not tensor.is_contiguous():
+            raise ValueError(f"{name}: device uploads need a contiguous CUDA {want} tensor")
+        shape = (ctypes.c_int64 * max(tensor.dim(), 1))(*tensor.shape)
+        dt = _lib.DTYPE_BF16 if self.dtype == "bf16" else _lib.DTYPE_F32
+        _lib.check(self._lib.clef_upload_device(self._handle, name.encode(), tensor.data_ptr(), dt, shape, tensor.dim()), self._handle)
+
     def finalize(self) -> None:
         _lib.check(self._lib.clef_finalize(self._handle), self._handle)
+
+    TIMING_CATEGORIES = ("embed", "rmsnorm", "gemm_qkv", "qk_norm_rope", "attention", "gemm_o", "gemm_gate_up", "gemm_down",
+                         "allreduce", "residual_add", "head", "other")
+
+    def set_timing(self, enable: bool) -> None:
+        _lib.check(self._lib.clef_set_timing(self._handle, int(enable)), self._handle)
+
+    def timing_report(self) -> dict[str, tuple[float, int]]:
+        """{category: (device ms, launches)} since the last report (see include/clef_b200.h)."""
+        n = len(self.TIMING_CATEGORIES)
+        ms = (ctypes.c_float * n)()
+        cnt = (ctypes.c_int * n)()
+        _lib.check(self._lib.clef_timing_report(self._handle, n, ms, cnt), self._handle)
+        return {c: (float(ms[i]), int(cnt[i])) for i, c in enumerate(self.TIMING_CATEGORIES)}
 
     @classmethod
     def from_arrays(

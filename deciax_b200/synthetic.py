@@ -65,6 +65,21 @@ def synthetic_weights(config: TextConfig, head: HeadConfig, seed: int, std: floa
                 "mlp.down_proj.weight": n(D, F),
             }
         )
+    return top, layers, _head_weights(rng, D, head, std, cast)
+
+
+def synthetic_head_weights(hidden_size: int, head: HeadConfig, seed: int, std: float = 0.02, dtype: str = "fp32"):
+    """Joint-head weights alone (the benchmark builds the backbone on the device)."""
+    cast = (lambda a: a.astype(ml_dtypes.bfloat16)) if dtype == "bf16" else (lambda a: a.astype(np.float32))
+    return _head_weights(np.random.default_rng(seed), hidden_size, head, std, cast)
+
+
+def _head_weights(rng, D: int, head: HeadConfig, std: float, cast):
+    W, FF = head.width, head.ffn
+
+    def n(*shape, s=std):
+        return cast(rng.standard_normal(shape, dtype=np.float32) * np.float32(s))
+
     hp = {}
 
     def ln(name, dim):
@@ -112,7 +127,7 @@ def synthetic_weights(config: TextConfig, head: HeadConfig, seed: int, std: floa
     hp["prior_logit_scale"] = cast(np.array(np.log(10.0), np.float32))
     hp["joint_logit_scale"] = cast(np.array(np.log(10.0), np.float32))
     hp["residual_gate"] = cast(np.array(0.0, np.float32))
-    return top, layers, hp
+    return hp
 
 
 @dataclass(frozen=True)

@@ -110,6 +110,11 @@ int clef_create(const ClefConfig* config, int device, int tp_rank, int tp_size, 
  * host_dtype: CLEF_DTYPE_F32 or CLEF_DTYPE_BF16 (raw bfloat16 bits). */
 int clef_upload(void* handle, const char* name, const void* host, int host_dtype, const int64_t* shape, int ndim);
 
+/* As clef_upload, with the source already in device memory of this handle's
+ * GPU and in the compute dtype (weights created or loaded on the device). */
+int clef_upload_device(void* handle, const char* name, const void* device_ptr, int dtype, const int64_t* shape,
+                       int ndim);
+
 /* Check every tensor is present and build the packed layouts. */
 int clef_finalize(void* handle);
 
@@ -138,6 +143,17 @@ int clef_reserve(void* handle, int b, int s, int lx, int o, int q);
  * kernel recorded since the last check (CLEF_EDEVICE: wait timeout or an
  * out-of-range token id).  clef_forward does this itself. */
 int clef_check_status(void* handle);
+
+/* Per-kernel device timing.  While enabled, every forward records a CUDA
+ * event after each launch on its stream; clef_timing_report synchronises and
+ * returns, per category, the summed milliseconds and launch count since the
+ * last report (then resets).  Categories: 0 embedding, 1 RMSNorm, 2 QKV GEMM,
+ * 3 q/k-norm+RoPE, 4 attention, 5 o-proj GEMM, 6 gate/up GEMM, 7 down GEMM,
+ * 8 NCCL all-reduce, 9 TP residual add, 10 lexical means + joint head,
+ * 11 other. */
+#define CLEF_TIMING_CATEGORIES 12
+int clef_set_timing(void* handle, int enable);
+int clef_timing_report(void* handle, int n, float* ms, int* launches);
 
 /* Number of kernels the last forward launched (for launch accounting). */
 int clef_last_launch_count(void* handle);

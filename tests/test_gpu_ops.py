@@ -62,12 +62,24 @@ def test_gemm_bf16_tcgen05(m, n, k, epi):
         out.copy_(dev(r, "bf16"))
         run_gemm("bf16", 2, A, B, out, n, res=out, ldr=n)  # in place, as the layer does
         expected = O.bf16(r + O.bf16(acc))
+        # Two roundings: T(acc) may round the other way when the fp32 sums differ
+        # in their last bits (one step of acc), and T(r + T(acc)) then rounds
+        # again (one step of the sum): two bf16 steps of the larger magnitude.
+        scale = 2 * (np.abs(r) + np.abs(acc))
     else:
         bias = O.bf16(rng.standard_normal(n).astype(F32)) if epi == "bias" else None
         run_gemm("bf16", 0, A, B, out, n, bias=dev(bias, "bf16") if bias is not None else None)
         expected = O.bf16(acc + (bias if bias is not None else 0))
+        scale = np.abs(expected)
     got = host(out)
-    np.testing.assert_allclose(got, expected, rtol=BF16_RTOL, atol=1e-3)
+    # One bf16 step of the output scale, plus a floor for the fp32 accumulation
+    # order (K products of magnitude ~0.05 summed in a different order).
+    tol = BF16_RTOL * scale + 1e-3
+    bad = np.abs(got - expected) > tol
+    if bad.any():
+        i = np.unravel_index(np.argmax(np.abs(got - expected) - tol), got.shape)
+        raise AssertionError(f"{bad.sum()} elements out of tolerance; worst at {i}: got {got[i]}, expected {expected[i]}, "
+                             f"fp32 acc {acc[i]}")
     assert np.mean(got != expected) < 0.02  # almost every element bit-identical
 
 
@@ -131,7 +143,8 @@ def test_rmsnorm(dtype, rows, dim):
     x = O.cast(rng.standard_normal((rows, dim)).astype(F32) * F32(3), dtype)
     w = O.cast(rng.standard_normal(dim).astype(F32) * F32(0.1), dtype)
     out = torch.empty((rows, dim), dtype=torch.bfloat16 if dtype == "bf16" else torch.float32, device="cuda")
-    _lib.check(lib().clef_op_rmsnorm(dt_code(dtype), ptr(dev(x, dtype)), ptr(dev(w, dtype)), ptr(out), rows, dim, 1e-6, None))
+    X, Wt = dev(x, dtype), dev(w, dtype)  # keep alive: the caching allocator would otherwise alias them
+    _lib.check(lib().clef_op_rmsnorm(dt_code(dtype), ptr(X), ptr(Wt), ptr(out), rows, dim, 1e-6, None))
     expected = O.rms(x, w, 1e-6, dtype)
     if dtype == "bf16":
         np.testing.assert_allclose(host(out), expected, rtol=BF16_RTOL, atol=1e-6)
@@ -149,7 +162,8 @@ def test_qk_norm_rope(dtype, d, prf):
     qw = O.cast(rng.standard_normal(d).astype(F32) * F32(0.1), dtype)
     kw = O.cast(rng.standard_normal(d).astype(F32) * F32(0.1), dtype)
     t = dev(qkv.reshape(b * s, n), dtype)
-    st = lib().clef_op_qk_norm_rope(dt_code(dtype), ptr(t), b, s, hq, hkv, d, prf, 10000.0, ptr(dev(qw, dtype)), ptr(dev(kw, dtype)), 1e-6, None)
+    QW, KW = dev(qw, dtype), dev(kw, dtype)  # keep alive: the caching allocator would otherwise alias them
+    st = lib().clef_op_qk_norm_rope(dt_code(dtype), ptr(t), b, s, hq, hkv, d, prf, 10000.0, ptr(QW), ptr(KW), 1e-6, None)
     _lib.check(st)
     got = host(t).reshape(b, s, n)
     raw = qkv[..., : hq * 2 * d].reshape(b, s, hq, 2 * d)
@@ -178,7 +192,8 @@ def attention_case(dtype, d, s, softcap=0.0, window=0, lengths=None, seed=0):
     mask = np.arange(s)[None] < np.array(lengths)[:, None]
     out = torch.zeros((b * s, hq * d), dtype=torch.bfloat16 if dtype == "bf16" else torch.float32, device="cuda")
     m = torch.from_numpy(mask.astype(np.uint8)).cuda()
-    st = lib().clef_op_attention(dt_code(dtype), ptr(dev(qkv.reshape(b * s, n), dtype)), ptr(m), ptr(out), b, s, hq, hkv, d, softcap, window, None)
+    QKV = dev(qkv.reshape(b * s, n), dtype)
+    st = lib().clef_op_attention(dt_code(dtype), ptr(QKV), ptr(m), ptr(out), b, s, hq, hkv, d, softcap, window, None)
     _lib.check(st)
     raw = qkv[..., : hq * 2 * d].reshape(b, s, hq, 2 * d)
     q, gate = raw[..., :d], raw[..., d:]
