@@ -36,6 +36,7 @@ EXPORTS = (
     "clef_op_gemm",
     "clef_op_rmsnorm",
     "clef_op_qk_norm_rope",
+    "clef_op_qk_norm_rope_noalloc",
     "clef_op_attention",
 )
 
@@ -135,6 +136,7 @@ def load() -> ctypes.CDLL:
             "clef_op_gemm": [i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp],
             "clef_op_rmsnorm": [i32, vp, vp, vp, i32, i32, f32, vp],
             "clef_op_qk_norm_rope": [i32, vp, i32, i32, i32, i32, i32, f32, f32, vp, vp, f32, vp],
+            "clef_op_qk_norm_rope_noalloc": [i32, vp, i32, i32, i32, i32, i32, f32, f32, vp, vp, f32, vp],
             "clef_op_attention": [i32, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp],
         }
         for name, args in sigs.items():

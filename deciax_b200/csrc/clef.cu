@@ -1647,3 +1647,95 @@ int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Allocation-free variant of clef_op_qk_norm_rope
+// ===========================================================================
+//
+// clef_op_qk_norm_rope builds its cos/sin tables in freshly allocated device
+// memory on every call.  Some callers cannot allocate device memory: a host
+// framework that owns every device buffer (an XLA/JAX FFI custom call gets
+// its inputs, outputs and workspace from XLA), or a serving loop that must not
+// run cudaMalloc/cudaFree because they can synchronise the whole device.  For
+// them, clef_op_qk_norm_rope_noalloc keeps the tables in a fixed array in the
+// library's own device memory instead.
+
+namespace clef {
+
+// cos table followed by sin table, each up to kNoAllocRopeEntries floats
+// (positions x rot/2): 2 x 4 MiB, resident on every GPU that loads the library.
+constexpr int kNoAllocRopeEntries = 1 << 20;
+static __device__ __align__(256) float g_noalloc_rope[2 * kNoAllocRopeEntries];
+
+struct RopeFreqs {
+  float inv[128];  // inverse frequencies, rot/2 <= 128 (head_dim <= 256)
+};
+
+// Fill cos/sin [s, half] from float32 angles pos * inv_freq, evaluated in
+// double precision like the host tables of clef_op_qk_norm_rope.
+__global__ void noalloc_rope_table_kernel(float* __restrict__ cos_t, float* __restrict__ sin_t, int s, int half,
+                                          RopeFreqs f) {
+  const long long n = static_cast<long long>(s) * half;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(i / half), j = static_cast<int>(i % half);
+    const float ang = static_cast<float>(p) * f.inv[j];
+    cos_t[i] = static_cast<float>(cos(static_cast<double>(ang)));
+    sin_t[i] = static_cast<float>(sin(static_cast<double>(ang)));
+  }
+}
+
+// Device address of g_noalloc_rope per device, looked up once per device with
+// that device current (the array's host-side name is not a device address).
+static float* noalloc_rope_scratch(int device) {
+  static std::mutex mu;
+  static std::map<int, float*> addr;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = addr.find(device);
+  if (it != addr.end()) return it->second;
+  float* p = nullptr;
+  CUDA_CHECK(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_rope));
+  addr[device] = p;
+  return p;
+}
+
+}  // namespace clef
+
+extern "C" int clef_op_qk_norm_rope_noalloc(int dtype, void* qkv, int b, int s, int hq, int hkv, int d,
+                                            float partial_rotary_factor, float rope_theta, const void* q_norm,
+                                            const void* k_norm, float eps, void* stream) {
+  return guarded(nullptr, [&] {
+    REQUIRE(qkv && q_norm && k_norm && b > 0 && s > 0 && hq > 0 && hkv > 0 && d > 0, "bad qk_norm_rope arguments");
+    REQUIRE(dtype == CLEF_DTYPE_BF16 || dtype == CLEF_DTYPE_F32, "bad dtype");
+    const int rot = static_cast<int>(d * partial_rotary_factor);
+    REQUIRE(rot > 0 && rot % 2 == 0 && rot <= d, "invalid partial rotary dimension");
+    const int half = rot / 2;
+    REQUIRE(half <= 128, "clef_op_qk_norm_rope_noalloc supports rot/2 <= 128 (head_dim <= 256)");
+    REQUIRE(static_cast<long long>(s) * half <= clef::kNoAllocRopeEntries,
+            "clef_op_qk_norm_rope_noalloc: seq_len * rot/2 exceeds its fixed table of 1048576 entries");
+    const int device = clef::current_device();
+    float* cos_t = clef::noalloc_rope_scratch(device);
+    float* sin_t = cos_t + clef::kNoAllocRopeEntries;
+    clef::RopeFreqs f{};
+    for (int i = 0; i < half; ++i)
+      f.inv[i] = 1.0f / powf(rope_theta, static_cast<float>(2 * i) / static_cast<float>(rot));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const long long n = static_cast<long long>(s) * half;
+    clef::noalloc_rope_table_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
+        cos_t, sin_t, s, half, f);
+    CUDA_CHECK(cudaGetLastError());
+    const int ld = hq * 2 * d + 2 * hkv * d;
+    const int Tt = b * s, warps = 8;
+    const long long items = static_cast<long long>(Tt) * (hq + hkv);
+    const int grid = static_cast<int>((items + warps - 1) / warps);
+    if (dtype == CLEF_DTYPE_BF16)
+      clef::qk_norm_rope_kernel<bf16><<<grid, warps * 32, warps * d * 4, st>>>(
+          static_cast<bf16*>(qkv), ld, Tt, s, hq, hkv, d, rot, static_cast<const bf16*>(q_norm),
+          static_cast<const bf16*>(k_norm), cos_t, sin_t, eps);
+    else
+      clef::qk_norm_rope_kernel<float><<<grid, warps * 32, warps * d * 4, st>>>(
+          static_cast<float*>(qkv), ld, Tt, s, hq, hkv, d, rot, static_cast<const float*>(q_norm),
+          static_cast<const float*>(k_norm), cos_t, sin_t, eps);
+    CUDA_CHECK(cudaGetLastError());
+  });
+}

@@ -182,6 +182,26 @@ int clef_op_rmsnorm(int dtype, const void* x, const void* w, void* out, int rows
 int clef_op_qk_norm_rope(int dtype, void* qkv, int b, int s, int hq, int hkv, int d, float partial_rotary_factor,
                          float rope_theta, const void* q_norm, const void* k_norm, float eps, void* stream);
 
+/* Allocation-free form of clef_op_qk_norm_rope (no counterpart in the reference).
+ * For callers that cannot allocate device memory themselves or through us: a
+ * host framework that owns every device buffer (e.g. an XLA FFI custom call,
+ * which receives all its memory from XLA), or a serving loop that must avoid
+ * cudaMalloc/cudaFree because they may synchronise the device.  Same
+ * arguments and result as clef_op_qk_norm_rope; the cos/sin tables live in a
+ * fixed 8 MiB array inside the library (held on every GPU that loads it until
+ * exit) instead of memory allocated per call.
+ *  - Limit: s * rot/2 <= 1048576 table entries and rot/2 <= 128
+ *    (rot = head_dim * partial_rotary_factor); larger sizes return CLEF_EINVAL.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - Every call rewrites the table entries it reads, so no state carries over
+ *    between calls, but all calls on a device share the one array: calls whose
+ *    kernels overlap on the GPU (e.g. on two streams) race. */
+int clef_op_qk_norm_rope_noalloc(int dtype, void* qkv, int b, int s, int hq, int hkv, int d,
+                                 float partial_rotary_factor, float rope_theta, const void* q_norm, const void* k_norm,
+                                 float eps, void* stream);
+
 /* Causal GQA attention with the sigmoid output gate over a packed projection
  * (kernels/attention/blocked.py:9-32, text.py:90-91): out [b*s, Hq*d]. */
 int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out, int b, int s, int hq, int hkv, int d,
