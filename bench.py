@@ -396,9 +396,91 @@ def gpu_arm(args) -> None:
         dist.destroy_process_group()
 
 
+def gemm_arm(args) -> None:
+    """BASELINE configs[2] ("cfg3"): the fused-QKV and fused gated-MLP GEMMs at
+    M=16384 through the kernel-level C ABI, reported as TFLOP/s.
+
+    x [16384, 3584] ~ N(0,1); W_qkv [8192, 3584] ((16+2x8)x256 rows, no gate,
+    as BASELINE states), W_gate|up packed [28672, 3584], W_down [3584, 14336],
+    all N(0, 0.02), seed 2, BF16.  One step = QKV GEMM + gate/up GEMM with the
+    SwiGLU epilogue + down GEMM with the residual epilogue.
+    """
+    import torch
+
+    from deciax_b200 import _lib
+    from deciax_b200.build import build as build_lib
+
+    build_lib()
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda:0")
+    gen.manual_seed(2)
+    M, D, F, NQ = 16384, 3584, 14336, (16 + 2 * 8) * 256
+
+    def randn(*shape, std):
+        return torch.empty(shape, dtype=torch.bfloat16, device="cuda").normal_(0.0, std, generator=gen)
+
+    x = randn(M, D, std=1.0)
+    w_qkv = randn(NQ, D, std=WEIGHT_STD)
+    w_gu = randn(2 * F, D, std=WEIGHT_STD)
+    w_down = randn(D, F, std=WEIGHT_STD)
+    qkv = torch.empty((M, NQ), dtype=torch.bfloat16, device="cuda")
+    act = torch.empty((M, F), dtype=torch.bfloat16, device="cuda")
+    y = torch.empty((M, D), dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    sp = stream.cuda_stream
+    B = _lib.DTYPE_BF16
+    events = []
+
+    def step(timed: bool) -> None:
+        calls = [(0, M, NQ, D, x, w_qkv, qkv, NQ, None, 0), (1, M, 2 * F, D, x, w_gu, act, F, None, 0),
+                 (2, M, D, F, act, w_down, y, D, y, D)]
+        for epi, m, n, k, a, b, out, ldo, res, ldr in calls:
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            _lib.check(lib.clef_op_gemm(B, epi, m, n, k, a.data_ptr(), b.data_ptr(), out.data_ptr(), ldo, None,
+                                        res.data_ptr() if res is not None else None, ldr, sp))
+            if timed:
+                e1.record(stream)
+                events.append((epi, e0, e1))
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    flops = {0: 2.0 * M * D * NQ, 1: 2.0 * M * D * 2 * F, 2: 2.0 * M * F * D}
+    per = {0: [], 1: [], 2: []}
+    for epi, e0, e1 in events:
+        per[epi].append(e0.elapsed_time(e1))
+    total = sum(flops.values())
+    peaks = measured_peaks()
+    names = {0: "qkv", 1: "gate_up_swiglu", 2: "down_residual"}
+    kern = {names[e]: {"ms": statistics.mean(v), "tflops": flops[e] / (statistics.mean(v) / 1e3) / 1e12} for e, v in per.items()}
+    value = total * args.steps / (ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": "cfg3 fused QKV + gated-MLP GEMM throughput (M=16384, BF16)", "value": value, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg3: x[16384,3584] N(0,1); W_qkv[8192,3584], W_gate|up[28672,3584], W_down[3584,14336] "
+                   "N(0,0.02) seed 2", "l2": "operands larger than L2 (1.3 GB per step)"},
+        "kernels": kern, "frac_of_measured_burst": value / peaks["bf16_tflops"],
+        "frac_of_measured_sustained": value / peaks["bf16_tflops_sustained"], "gpu_launches": 3 * args.steps,
+        "clocks": clocks.summary(),
+    }), flush=True)
+
+
 def traffic_per_launch():
     """DRAM bytes per gate/up launch from the committed ncu summary, if present."""
-    p = ROOT / "profiles" / "gemm_gate_up_cfg2.md"
+    p = ROOT / "profiles" / "gemm_gate_up_m16384.md"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -414,9 +496,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("cfg2", "cfg3"), default="cfg2",
+                    help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.workload == "cfg3":
+        gemm_arm(args)
     else:
         gpu_arm(args)
 
