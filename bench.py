@@ -478,6 +478,50 @@ def gemm_arm(args) -> None:
     }), flush=True)
 
 
+def attention_arm(args) -> None:
+    """cfg2's attention layer alone: causal GQA over a packed projection of
+    8 x 2048 tokens, 16 query / 8 key-value heads of 256, with the sigmoid
+    gate, through clef_op_attention; TFLOP/s counts causal pairs only."""
+    import torch
+
+    from deciax_b200 import _lib
+    from deciax_b200.build import build as build_lib
+
+    build_lib()
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    gen = torch.Generator(device="cuda:0")
+    gen.manual_seed(3)
+    B, S, H, HK, Dh = STATES, SEQ, CFG2["num_attention_heads"], CFG2["num_key_value_heads"], CFG2["head_dim"]
+    n = H * 2 * Dh + 2 * HK * Dh
+    qkv = torch.empty((B * S, n), dtype=torch.bfloat16, device="cuda").normal_(0.0, 1.0, generator=gen)
+    mask = torch.ones((B, S), dtype=torch.uint8, device="cuda")
+    out = torch.empty((B * S, H * Dh), dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def run():
+        _lib.check(lib.clef_op_attention(_lib.DTYPE_BF16, qkv.data_ptr(), mask.data_ptr(), out.data_ptr(), B, S, H, HK, Dh,
+                                         0.0, 0, stream.cuda_stream))
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        run()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    flops = 2.0 * H * Dh * S * (S + 1) * B
+    peaks = measured_peaks()
+    print(json.dumps({"metric": "cfg2 attention layer throughput (B8 S2048 16q/8kv x256, causal, gated)",
+                      "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps,
+                      "warmup": args.warmup, "frac_of_measured_burst": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                      "dtype": "bf16", "data": "synthetic", "gpu_launches": args.steps}), flush=True)
+
+
 def traffic_per_launch():
     """DRAM bytes per gate/up launch from the committed ncu summary, if present."""
     p = ROOT / "profiles" / "gemm_gate_up_m16384.md"
@@ -496,13 +540,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("cfg2", "cfg3"), default="cfg2",
-                    help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark")
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "attention"), default="cfg2",
+                    help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark; "
+                    "attention = cfg2's attention layer alone")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
     elif args.workload == "cfg3":
         gemm_arm(args)
+    elif args.workload == "attention":
+        attention_arm(args)
     else:
         gpu_arm(args)
 

@@ -40,6 +40,9 @@ struct AttnArgs {
   float softcap;
   int window;
   int* status;
+  // q, k, v and gate are column offsets of one row-major [B*L, ldq] buffer
+  // starting at q (the packed QKV projection); enables the tcgen05 kernel.
+  int packed;
 };
 
 __device__ __forceinline__ float attn_score_transform(float s, float softcap) {

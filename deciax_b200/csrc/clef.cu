@@ -31,6 +31,7 @@
 
 #include "../../include/clef_b200.h"
 #include "attention.cuh"
+#include "attention_sm100.cuh"
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 #include "head.cuh"
@@ -294,10 +295,68 @@ static void attention(Launcher& L, const AttnArgs<T>& a) {
   REQUIRE(a.Hk > 0 && a.H % a.Hk == 0, "query heads must be a multiple of key/value heads");
   bool done = false;
   if constexpr (sizeof(T) == 2) {
+    // tcgen05 flash attention over the packed QKV projection
+    const long long kc = a.k - a.q, vc = a.v - a.q;
+    const bool tc_ok = a.packed && a.causal && (a.hd == 64 || a.hd == 128 || a.hd == 256) && a.Lq == a.Lk &&
+                       a.ldq == a.ldk && a.ldk == a.ldv && a.hsk == a.hsv && a.ldq % 8 == 0 && a.hsq % 64 == 0 &&
+                       a.hsk % 64 == 0 && kc % 64 == 0 && vc % 64 == 0 && aligned16(a.q) && a.ldo % 8 == 0 &&
+                       a.hso % 8 == 0 &&
+                       (!a.gate || (a.ldg == a.ldq && a.hsg == a.hsq && (a.gate - a.q) % 64 == 0 && a.gate > a.q));
+    if (tc_ok) {
+      AttnTcArgs t{};
+      t.B = a.B;
+      t.S = a.Lq;
+      t.H = a.H;
+      t.Hk = a.Hk;
+      t.q_col = 0;
+      t.k_col = static_cast<int>(kc);
+      t.v_col = static_cast<int>(vc);
+      t.g_col = a.gate ? static_cast<int>(a.gate - a.q) : 0;
+      t.hsq = static_cast<int>(a.hsq);
+      t.hsk = static_cast<int>(a.hsk);
+      t.gate = a.gate;
+      t.ldg = a.ldg;
+      t.out = a.out;
+      t.ldo = a.ldo;
+      t.hso = a.hso;
+      t.key_mask = a.key_mask;
+      t.mask_vec = a.key_mask && aligned16(a.key_mask) && a.Lk % 16 == 0;
+      t.softcap = a.softcap;
+      t.window = a.window;
+      t.status = a.status;
+      const CUtensorMap map = tmap_bf16(a.q, static_cast<uint64_t>(a.B) * a.Lq, a.ldq, a.ldq, 64);
+      // Output through TMA bulk stores when every 128-row tile stays inside one sequence.
+      t.tma_store = a.Lq % 128 == 0 && aligned16(a.out) && a.hso % 64 == 0;
+      const CUtensorMap out_map =
+          t.tma_store ? tmap_bf16(a.out, static_cast<uint64_t>(a.B) * a.Lq, a.ldo, a.ldo, 64) : map;
+      dim3 grid((a.Lq + 127) / 128, a.H, a.B);
+      static std::mutex mu_tc;
+      static std::set<std::pair<int, int>> done_tc;
+      const int dev = current_device();
+      auto launch = [&](auto kern, size_t smem, int hd) {
+        {
+          std::lock_guard<std::mutex> lock(mu_tc);
+          if (!done_tc.count({dev, hd})) {
+            CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+            done_tc.insert({dev, hd});
+          }
+        }
+        kern<<<grid, 192, smem, L.stream>>>(map, out_map, t);
+      };
+      if (a.hd == 64)
+        launch(attn_tc_kernel<64>, AttnTcShape<64>::SMEM, 64);
+      else if (a.hd == 128)
+        launch(attn_tc_kernel<128>, AttnTcShape<128>::SMEM, 128);
+      else
+        launch(attn_tc_kernel<256>, AttnTcShape<256>::SMEM, 256);
+      done = true;
+    }
+  }
+  if constexpr (sizeof(T) == 2) {
     const bool vec_ok = a.ldq % 8 == 0 && a.ldk % 8 == 0 && a.ldv % 8 == 0 && a.hsq % 8 == 0 && a.hsk % 8 == 0 &&
                         a.hsv % 8 == 0 && aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && a.ldo % 2 == 0 &&
                         a.hso % 2 == 0 && (!a.gate || (a.ldg % 2 == 0 && a.hsg % 2 == 0));
-    if (vec_ok && (a.hd == 64 || a.hd == 128 || a.hd == 256)) {
+    if (!done && vec_ok && (a.hd == 64 || a.hd == 128 || a.hd == 256)) {
       dim3 grid((a.Lq + 63) / 64, a.H, a.B);
       static std::mutex mu;
       static std::set<std::pair<int, int>> done_attr;
@@ -1004,6 +1063,7 @@ struct Model {
         a.softcap = cfg.attn_softcap;
         a.window = layer_window[li];
         a.status = Lc.status;
+        a.packed = 1;
         Lc.cat = kCatAttention;
         attention<T>(Lc, a);
       }
@@ -1637,6 +1697,7 @@ int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out
       a.softcap = softcap;
       a.window = window;
       a.status = nullptr;
+      a.packed = 1;
       clef::attention<T>(L, a);
     };
     if (dtype == CLEF_DTYPE_BF16)

@@ -60,7 +60,7 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n,
   n = r / gm;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_fast(x); }
 
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t taddr, int row, int n) {
