@@ -34,6 +34,7 @@ EXPORTS = (
     "clef_destroy",
     "clef_last_error",
     "clef_op_gemm",
+    "clef_op_gemm_qkv",
     "clef_op_rmsnorm",
     "clef_op_qk_norm_rope",
     "clef_op_qk_norm_rope_noalloc",
@@ -134,6 +135,7 @@ def load() -> ctypes.CDLL:
             "clef_last_launch_count": [vp],
             "clef_destroy": [vp],
             "clef_op_gemm": [i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp],
+            "clef_op_gemm_qkv": [vp, vp, vp, i32, i32, i32, i32, i32, f32, f32, i32, vp, vp, f32, vp],
             "clef_op_rmsnorm": [i32, vp, vp, vp, i32, i32, f32, vp],
             "clef_op_qk_norm_rope": [i32, vp, i32, i32, i32, i32, i32, f32, f32, vp, vp, f32, vp],
             "clef_op_qk_norm_rope_noalloc": [i32, vp, i32, i32, i32, i32, i32, f32, f32, vp, vp, f32, vp],

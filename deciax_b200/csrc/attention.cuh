@@ -43,7 +43,15 @@ struct AttnArgs {
   // q, k, v and gate are column offsets of one row-major [B*L, ldq] buffer
   // starting at q (the packed QKV projection); enables the tcgen05 kernel.
   int packed;
+  // the gate slots already hold T(sigmoid(T(gate))) (QKV GEMM epilogue)
+  int gate_presig;
 };
+
+// T(sigmoid(g)) of a raw gate, or the value itself when it was precomputed.
+template <typename T>
+__device__ __forceinline__ float gate_factor(float g, int presig) {
+  return presig ? g : round_to<T>(sigmoidf_exact(g));
+}
 
 __device__ __forceinline__ float attn_score_transform(float s, float softcap) {
   return softcap > 0.f ? softcap * tanhf(s / softcap) : s;
@@ -129,7 +137,7 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnArgs<T> a) {
     const int col = lane + 32 * c;
     if (col < hd) {
       float val = round_to<T>(o[c]);
-      if (grow) val = val * round_to<T>(sigmoidf_exact(to_f32(grow[col])));
+      if (grow) val = val * gate_factor<T>(to_f32(grow[col]), a.gate_presig);
       orow[col] = from_f32<T>(val);
     }
   }
@@ -364,8 +372,8 @@ __global__ void __launch_bounds__(128, 2) attn_fa2_bf16_kernel(AttnArgs<__nv_bfl
       float v1 = round_to<__nv_bfloat16>(o[j][2 * r + 1] * inv[r]);
       if (grow) {
         const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(grow + col);
-        v0 *= round_to<__nv_bfloat16>(sigmoidf_exact(__low2float(g)));
-        v1 *= round_to<__nv_bfloat16>(sigmoidf_exact(__high2float(g)));
+        v0 *= gate_factor<__nv_bfloat16>(__low2float(g), a.gate_presig);
+        v1 *= gate_factor<__nv_bfloat16>(__high2float(g), a.gate_presig);
       }
       *reinterpret_cast<uint32_t*>(orow + col) = pack_bf16x2(v0, v1);
     }

@@ -40,6 +40,7 @@ struct AttnTcArgs {
   const uint8_t* key_mask;  // [B, S] or nullptr
   int mask_vec;             // key_mask rows are 16-byte aligned and S % 16 == 0
   int tma_store;            // S % 128 == 0: every 128-row tile lies inside one sequence (tmap_out valid)
+  int gate_presig;          // gate slots hold T(sigmoid(T(gate))) already
   float softcap;
   int window;
   int* status;
@@ -443,8 +444,9 @@ __global__ void __launch_bounds__(192, 1)
               const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
               const float x0 = round_to<__nv_bfloat16>(__uint_as_float(o[v4 * 8 + 2 * e]) * inv);
               const float x1 = round_to<__nv_bfloat16>(__uint_as_float(o[v4 * 8 + 2 * e + 1]) * inv);
-              w[e] = pack_bf16x2(x0 * round_to<__nv_bfloat16>(sigmoid_fast(g.x)),
-                                 x1 * round_to<__nv_bfloat16>(sigmoid_fast(g.y)));
+              const float s0 = a.gate_presig ? g.x : round_to<__nv_bfloat16>(sigmoid_fast(g.x));
+              const float s1 = a.gate_presig ? g.y : round_to<__nv_bfloat16>(sigmoid_fast(g.y));
+              w[e] = pack_bf16x2(x0 * s0, x1 * s1);
             }
           } else {
 #pragma unroll

@@ -256,6 +256,37 @@ static void gemm_bf16(Launcher& L, int epi, const bf16* A, int lda, const bf16* 
   L.tick();
 }
 
+// Parameters of the fused QKV epilogue (q/k-norm + partial RoPE, sigmoid of the gate).
+struct QkvFusion {
+  const bf16* q_norm;
+  const bf16* k_norm;
+  const float* rope_cos;
+  const float* rope_sin;
+  int hq, hkv, head_dim, rot, seq;
+  float eps;
+};
+
+// Whether the QKV projection can carry the fused epilogue: every 256-column
+// tile must hold whole heads and the rotated half must be whole 32-column chunks.
+static bool qkv_fusable(int head_dim, int rot) {
+  return (head_dim == 64 || head_dim == 128 || head_dim == 256) && rot % 64 == 0;
+}
+
+static void gemm_bf16_qkv(Launcher& L, const bf16* A, int lda, const bf16* B, int ldb, int M, int N, int K, bf16* out,
+                          int ldo, const QkvFusion& f) {
+  REQUIRE(M > 0 && N > 0 && K > 0, "GEMM dimensions must be positive");
+  REQUIRE(K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && ldo % 8 == 0, "bf16 GEMM needs strides multiple of 8");
+  REQUIRE(aligned16(A) && aligned16(B) && aligned16(out), "bf16 GEMM operands must be 16-byte aligned");
+  REQUIRE(qkv_fusable(f.head_dim, f.rot), "fused QKV epilogue needs head_dim in {64,128,256} and rot % 64 == 0");
+  REQUIRE(N == f.hq * 2 * f.head_dim + 2 * f.hkv * f.head_dim, "fused QKV epilogue: N does not match the heads");
+  GemmArgs args{M, N, K, out, ldo, nullptr, nullptr, 0, L.status, f.q_norm, f.k_norm, f.rope_cos, f.rope_sin,
+                f.hq, f.hkv, f.head_dim, f.rot, f.seq, f.eps};
+  const CUtensorMap ta = tmap_bf16(A, M, K, lda, 128);
+  const CUtensorMap tb = tmap_bf16(B, N, K, ldb, 256);
+  launch_tc_gemm<256, kEpiQkv>(ta, tb, args, L.stream);
+  L.tick();
+}
+
 template <typename T>
 static void gemm_simt(Launcher& L, int epi, const T* A, int lda, const T* B, int ldb, int M, int N, int K, void* out,
                       int ldo, const T* bias, const T* res, int ldr) {
@@ -321,6 +352,7 @@ static void attention(Launcher& L, const AttnArgs<T>& a) {
       t.hso = a.hso;
       t.key_mask = a.key_mask;
       t.mask_vec = a.key_mask && aligned16(a.key_mask) && a.Lk % 16 == 0;
+      t.gate_presig = a.gate_presig;
       t.softcap = a.softcap;
       t.window = a.window;
       t.status = a.status;
@@ -1021,11 +1053,20 @@ struct Model {
       Lc.cat = kCatNorm;
       rmsnorm<T>(Lc, x, D, l.w_in.as<T>(), hbuf, D, Tt, D, eps);
       Lc.cat = kCatGemmQkv;
-      if constexpr (sizeof(T) == 2)
-        gemm_bf16(Lc, kEpiStore, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
-      else
+      bool fused_qkv = false;
+      if constexpr (sizeof(T) == 2) {
+        if (qkv_fusable(d, rot)) {
+          const QkvFusion f{l.q_norm.as<bf16>(), l.k_norm.as<bf16>(), rope_cos.as<float>(), rope_sin.as<float>(),
+                            Hq_l,           Hkv_l,  d,  rot, S, eps};
+          gemm_bf16_qkv(Lc, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, f);
+          fused_qkv = true;
+        } else {
+          gemm_bf16(Lc, kEpiStore, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
+        }
+      } else {
         gemm_simt<T>(Lc, kSimtStore, hbuf, D, l.w_qkv.as<T>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
-      {
+      }
+      if (!fused_qkv) {
         const int warps = 8;
         const long long items = static_cast<long long>(Tt) * (Hq_l + Hkv_l);
         qk_norm_rope_kernel<T><<<static_cast<int>((items + warps - 1) / warps), warps * 32, warps * d * 4, st>>>(
@@ -1064,6 +1105,7 @@ struct Model {
         a.window = layer_window[li];
         a.status = Lc.status;
         a.packed = 1;
+        a.gate_presig = fused_qkv ? 1 : 0;
         Lc.cat = kCatAttention;
         attention<T>(Lc, a);
       }
@@ -1616,6 +1658,32 @@ int clef_op_gemm(int dtype, int epi, int M, int N, int K, const void* A, const v
     } else {
       throw Error(CLEF_EINVAL, "bad dtype");
     }
+  });
+}
+
+int clef_op_gemm_qkv(const void* A, const void* B, void* out, int M, int K, int hq, int hkv, int d,
+                     float partial_rotary_factor, float rope_theta, int seq, const void* q_norm, const void* k_norm,
+                     float eps, void* stream) {
+  return guarded(nullptr, [&] {
+    REQUIRE(A && B && out && q_norm && k_norm && M > 0 && K > 0 && hq > 0 && hkv > 0 && d > 0 && seq > 0,
+            "bad fused QKV GEMM arguments");
+    const int rot = static_cast<int>(d * partial_rotary_factor);
+    REQUIRE(rot > 0 && rot % 2 == 0 && rot <= d, "invalid partial rotary dimension");
+    REQUIRE(M % seq == 0, "rows must be whole sequences of length seq");
+    std::vector<float> cs, sn;
+    clef::rope_tables(seq, rot, rope_theta, cs, sn);
+    clef::DBuf dc, ds;
+    dc.alloc(cs.size() * 4);
+    ds.alloc(sn.size() * 4);
+    CUDA_CHECK(cudaMemcpy(dc.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(ds.p, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    const int N = hq * 2 * d + 2 * hkv * d;
+    clef::Launcher L{static_cast<cudaStream_t>(stream), nullptr, 0};
+    const clef::QkvFusion f{static_cast<const bf16*>(q_norm), static_cast<const bf16*>(k_norm), dc.as<float>(),
+                            ds.as<float>(), hq, hkv, d, rot, seq, eps};
+    clef::gemm_bf16_qkv(L, static_cast<const bf16*>(A), K, static_cast<const bf16*>(B), K, M, N, K,
+                        static_cast<bf16*>(out), N, f);
+    CUDA_CHECK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));  // the tables are freed on return
   });
 }
 

@@ -26,7 +26,7 @@
 
 namespace clef {
 
-enum GemmEpi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2, kEpiF32 = 3 };
+enum GemmEpi : int { kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2, kEpiF32 = 3, kEpiQkv = 4 };
 
 struct GemmArgs {
   int M, N, K;
@@ -36,6 +36,15 @@ struct GemmArgs {
   const __nv_bfloat16* residual;   // [M, ldr] (kEpiResidual)
   int ldr;
   int* status;
+  // kEpiQkv: the packed projection [Hq x (q d | gate d)] [Hkv x k d] [Hkv x v d]
+  // leaves with q/k RMSNorm(1+w) + partial RoPE applied (text.py:83-88) and
+  // the gate replaced by T(sigmoid(T(gate))) (text.py:91); v unchanged.
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* rope_cos;  // [seq, rot/2]
+  const float* rope_sin;
+  int hq, hkv, head_dim, rot, seq;
+  float eps;
 };
 
 template <int BN>
@@ -62,10 +71,131 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n,
 
 __device__ __forceinline__ float silu_f(float x) { return x * sigmoid_fast(x); }
 
+__device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    reinterpret_cast<uint4*>(dst)[q] =
+        make_uint4(pack_bf16x2(v[8 * q + 0], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                   pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+}
+
+__device__ __forceinline__ void load32_bf16(const __nv_bfloat16* src, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = reinterpret_cast<const uint4*>(src)[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      v[8 * q + 2 * e] = f.x;
+      v[8 * q + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void load32_f32(const float* src, float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 f = reinterpret_cast<const float4*>(src)[q];
+    v[4 * q] = f.x;
+    v[4 * q + 1] = f.y;
+    v[4 * q + 2] = f.z;
+    v[4 * q + 3] = f.w;
+  }
+}
+
+// kEpiQkv: the tile holds whole heads (head_dim divides BN).  Thread = row.
+template <int BN>
+__device__ __forceinline__ void qkv_epilogue(const GemmArgs& a, uint32_t taddr, int row, int n) {
+  using bf = __nv_bfloat16;
+  const bool live = row < a.M;
+  const int d = a.head_dim, half = a.rot / 2;
+  const int qcols = a.hq * 2 * d, kend = qcols + a.hkv * d;
+  const int pos = live ? row % a.seq : 0;
+  bf* out_row = static_cast<bf*>(a.out) + static_cast<size_t>(live ? row : 0) * a.ldo;
+#pragma unroll 1
+  for (int seg = 0; seg < BN; seg += d) {
+    const int col = n * BN + seg;  // first column of this head segment (uniform across the warp)
+    if (col >= a.N) break;
+    const bool gate = col < qcols && (col % (2 * d)) >= d;
+    const bool is_k = col >= qcols && col < kend;
+    const bool norm = (col < qcols && !gate) || is_k;
+    if (!norm) {  // v: T(x); gate: T(sigmoid(T(x)))
+#pragma unroll 1
+      for (int c = 0; c < d; c += 32) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(taddr + seg + c, r);
+        tmem_wait_ld();
+        if (live) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = round_to<bf>(__uint_as_float(r[j]));
+            v[j] = gate ? sigmoid_fast(x) : x;
+          }
+          store32_bf16(out_row + col + c, v);
+        }
+      }
+      continue;
+    }
+    // RMSNorm over the head of T(x), scaling by (1 + w)
+    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+    for (int c = 0; c < d; c += 32) {
+      uint32_t r[32];
+      __syncwarp();
+      tmem_ld32(taddr + seg + c, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = round_to<bf>(__uint_as_float(r[j]));
+        ps[j & 3] = fmaf(x, x, ps[j & 3]);
+      }
+    }
+    const float rs = rsqrtf(((ps[0] + ps[1]) + (ps[2] + ps[3])) / static_cast<float>(d) + a.eps);
+    const bf* w = is_k ? a.k_norm : a.q_norm;
+#pragma unroll 1
+    for (int c = 0; c < d; c += 32) {
+      if (c >= half && c < a.rot) continue;  // written together with its rotate-half partner
+      uint32_t ra[32];
+      float wa[32], ya[32];
+      __syncwarp();
+      tmem_ld32(taddr + seg + c, ra);
+      tmem_wait_ld();
+      load32_bf16(w + c, wa);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ya[j] = round_to<bf>(round_to<bf>(__uint_as_float(ra[j])) * rs * (wa[j] + 1.f));
+      if (c < half) {
+        uint32_t rb[32];
+        float wb[32], yb[32], cs[32], sn[32];
+        tmem_ld32(taddr + seg + c + half, rb);
+        tmem_wait_ld();
+        load32_bf16(w + c + half, wb);
+        load32_f32(a.rope_cos + static_cast<size_t>(pos) * half + c, cs);
+        load32_f32(a.rope_sin + static_cast<size_t>(pos) * half + c, sn);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          yb[j] = round_to<bf>(round_to<bf>(__uint_as_float(rb[j])) * rs * (wb[j] + 1.f));
+          const float co = round_to<bf>(cs[j]), si = round_to<bf>(sn[j]);
+          const float lo = round_to<bf>(round_to<bf>(ya[j] * co) + round_to<bf>(-yb[j] * si));
+          const float hi = round_to<bf>(round_to<bf>(yb[j] * co) + round_to<bf>(ya[j] * si));
+          ya[j] = lo;
+          yb[j] = hi;
+        }
+        if (live) store32_bf16(out_row + col + c + half, yb);
+      }
+      if (live) store32_bf16(out_row + col + c, ya);
+    }
+  }
+}
+
 template <int BN, int EPI>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, uint32_t taddr, int row, int n) {
   const bool live = row < a.M;
-  if constexpr (EPI == kEpiSwiglu) {
+  if constexpr (EPI == kEpiQkv) {
+    qkv_epilogue<BN>(a, taddr, row, n);
+  } else if constexpr (EPI == kEpiSwiglu) {
     // Tile n covers packed columns [n*BN, n*BN+BN): gate j at c, up j at c + BN/2.
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
 #pragma unroll 1

@@ -174,6 +174,16 @@ const char* clef_last_error(void* handle);
 int clef_op_gemm(int dtype, int epi, int M, int N, int K, const void* A, const void* B, void* out, int ldo,
                  const void* bias, const void* residual, int ldr, void* stream);
 
+/* The QKV projection with its fused epilogue, bf16 (tcgen05): out[M, N] with
+ * N = hq*2d + 2*hkv*d = A[M,K] B[N,K]^T where each query head's q and each
+ * key head leave RMSNorm(1+w)-normalised with partial RoPE at positions
+ * row % seq (models/qwen3_5/text.py:79-88), each gate leaves as
+ * T(sigmoid(T(gate))) (text.py:91) and v is unchanged.  Needs d in
+ * {64, 128, 256} and d * partial_rotary_factor a multiple of 64. */
+int clef_op_gemm_qkv(const void* A, const void* B, void* out, int M, int K, int hq, int hkv, int d,
+                     float partial_rotary_factor, float rope_theta, int seq, const void* q_norm, const void* k_norm,
+                     float eps, void* stream);
+
 /* RMSNorm scaling by (1 + w) (models/qwen3_5/text.py:25-28). */
 int clef_op_rmsnorm(int dtype, const void* x, const void* w, void* out, int rows, int dim, float eps, void* stream);
 

@@ -103,6 +103,41 @@ def test_gemm_bf16_swiglu_epilogue(m, f, k):
     np.testing.assert_allclose(host(out), expected, rtol=2 * BF16_RTOL, atol=2e-3)
 
 
+@pytest.mark.parametrize("d,prf,hq,hkv", [(256, 0.25, 2, 1), (128, 0.5, 4, 2), (64, 1.0, 4, 2), (256, 1.0, 1, 1)])
+def test_gemm_qkv_fused_epilogue(d, prf, hq, hkv):
+    """QKV GEMM + q/k RMSNorm + partial RoPE + sigmoid(gate) in the epilogue vs the oracle."""
+    import torch
+
+    rng = np.random.default_rng(d + hq)
+    b, s, k = 2, 128, 256
+    n = hq * 2 * d + 2 * hkv * d
+    x = O.bf16(rng.standard_normal((b * s, k)).astype(F32))
+    w = O.bf16(rng.standard_normal((n, k)).astype(F32) * F32(0.1))
+    qw = O.bf16(rng.standard_normal(d).astype(F32) * F32(0.1))
+    kw = O.bf16(rng.standard_normal(d).astype(F32) * F32(0.1))
+    X, Wt, QW, KW = dev(x, "bf16"), dev(w, "bf16"), dev(qw, "bf16"), dev(kw, "bf16")
+    out = torch.zeros((b * s, n), dtype=torch.bfloat16, device="cuda")
+    st = lib().clef_op_gemm_qkv(ptr(X), ptr(Wt), ptr(out), b * s, k, hq, hkv, d, prf, 10000.0, s, ptr(QW), ptr(KW), 1e-6, None)
+    _lib.check(st)
+    got = host(out).reshape(b, s, n)
+    proj = O.bf16(x.astype(np.float64) @ w.T.astype(np.float64)).reshape(b, s, n)
+    raw = proj[..., : hq * 2 * d].reshape(b, s, hq, 2 * d)
+    q, gate = raw[..., :d], raw[..., d:]
+    kk = proj[..., hq * 2 * d : hq * 2 * d + hkv * d].reshape(b, s, hkv, d)
+    v = proj[..., hq * 2 * d + hkv * d :]
+    q, kk = O.rms(q, qw, 1e-6, "bf16"), O.rms(kk, kw, 1e-6, "bf16")
+    rot = int(d * prf)
+    inv = O.rope_inv_freq(rot, 10000.0)
+    q = np.concatenate((O.apply_rope(q[..., :rot], inv, "bf16"), q[..., rot:]), -1)
+    kk = np.concatenate((O.apply_rope(kk[..., :rot], inv, "bf16"), kk[..., rot:]), -1)
+    got_raw = got[..., : hq * 2 * d].reshape(b, s, hq, 2 * d)
+    tol = dict(rtol=2 * BF16_RTOL, atol=1e-2)
+    np.testing.assert_allclose(got_raw[..., :d], q, **tol)
+    np.testing.assert_allclose(got_raw[..., d:], O.bf16(O.sigmoid(gate)), **tol)
+    np.testing.assert_allclose(got[..., hq * 2 * d : hq * 2 * d + hkv * d].reshape(b, s, hkv, d), kk, **tol)
+    np.testing.assert_allclose(got[..., hq * 2 * d + hkv * d :], v, rtol=BF16_RTOL, atol=1e-3)
+
+
 @pytest.mark.parametrize("epi", ["store", "residual", "f32"])
 def test_gemm_f32_simt(epi):
     import torch
