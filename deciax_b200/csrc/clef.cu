@@ -34,6 +34,7 @@
 #include "attention_sm100.cuh"
 #include "common.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm2_sm100.cuh"
 #include "head.cuh"
 #include "simt.cuh"
 
@@ -223,7 +224,46 @@ static void launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const G
   CUDA_CHECK(cudaGetLastError());
 }
 
-// bf16 GEMM on tcgen05.  A [M, K] (lda), B [N, K] (ldb).
+// Launch the CTA-pair GEMM: clusters of 2, as many as can be resident at once.
+template <int EPI>
+static void launch_tc_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, cudaStream_t st) {
+  using S = Gemm2Shape;
+  auto kern = gemm_bf16_sm100_pair<EPI>;
+  static std::mutex mu;
+  static std::map<int, int> max_clusters;
+  const int dev = current_device();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = S::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = max_clusters.find(dev);
+    if (it == max_clusters.end()) {
+      CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(S::SMEM)));
+      cfg.gridDim = dim3(2 * sm_count(dev) / 2);
+      int n = 0;
+      CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      REQUIRE(n > 0, "no CTA-pair cluster fits on this device");
+      it = max_clusters.emplace(dev, n).first;
+    }
+    clusters = it->second;
+  }
+  const int tiles = ((args.M + S::BM - 1) / S::BM) * ((args.N + S::BN - 1) / S::BN);
+  cfg.gridDim = dim3(2 * std::min(tiles, clusters));
+  CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+}
+
+// bf16 GEMM on tcgen05.  A [M, K] (lda), B [N, K] (ldb).  Large problems run
+// on CTA pairs (256x256 tiles); small ones on single CTAs.
 static void gemm_bf16(Launcher& L, int epi, const bf16* A, int lda, const bf16* B, int ldb, int M, int N, int K,
                       void* out, int ldo, const bf16* bias, const bf16* res, int ldr) {
   REQUIRE(M > 0 && N > 0 && K > 0, "GEMM dimensions must be positive");
@@ -233,6 +273,19 @@ static void gemm_bf16(Launcher& L, int epi, const bf16* A, int lda, const bf16* 
   if (epi == kEpiResidual) REQUIRE(res && aligned16(res) && ldr % 8 == 0, "residual operand must be aligned");
   if (epi == kEpiSwiglu) REQUIRE(N % 256 == 0, "SwiGLU GEMM needs N = 2F with F a multiple of 128");
   GemmArgs args{M, N, K, out, ldo, bias, res, ldr, L.status};
+  if (M >= 256 && N >= 256) {
+    const CUtensorMap ta = tmap_bf16(A, M, K, lda, 128);
+    const CUtensorMap tb = tmap_bf16(B, N, K, ldb, 128);
+    switch (epi) {
+      case kEpiStore: launch_tc_gemm_pair<kEpiStore>(ta, tb, args, L.stream); break;
+      case kEpiSwiglu: launch_tc_gemm_pair<kEpiSwiglu>(ta, tb, args, L.stream); break;
+      case kEpiResidual: launch_tc_gemm_pair<kEpiResidual>(ta, tb, args, L.stream); break;
+      case kEpiF32: launch_tc_gemm_pair<kEpiF32>(ta, tb, args, L.stream); break;
+      default: throw Error(CLEF_EINVAL, "bad GEMM epilogue");
+    }
+    L.tick();
+    return;
+  }
   const bool narrow = N <= 128 && epi != kEpiSwiglu;
   const int bn = narrow ? 128 : 256;
   const CUtensorMap ta = tmap_bf16(A, M, K, lda, 128);
@@ -282,8 +335,13 @@ static void gemm_bf16_qkv(Launcher& L, const bf16* A, int lda, const bf16* B, in
   GemmArgs args{M, N, K, out, ldo, nullptr, nullptr, 0, L.status, f.q_norm, f.k_norm, f.rope_cos, f.rope_sin,
                 f.hq, f.hkv, f.head_dim, f.rot, f.seq, f.eps};
   const CUtensorMap ta = tmap_bf16(A, M, K, lda, 128);
-  const CUtensorMap tb = tmap_bf16(B, N, K, ldb, 256);
-  launch_tc_gemm<256, kEpiQkv>(ta, tb, args, L.stream);
+  if (M >= 256 && N >= 256) {
+    const CUtensorMap tb = tmap_bf16(B, N, K, ldb, 128);
+    launch_tc_gemm_pair<kEpiQkv>(ta, tb, args, L.stream);
+  } else {
+    const CUtensorMap tb = tmap_bf16(B, N, K, ldb, 256);
+    launch_tc_gemm<256, kEpiQkv>(ta, tb, args, L.stream);
+  }
   L.tick();
 }
 
