@@ -1,0 +1,120 @@
+"""Tensor parallelism across GPUs: every rank holds a shard (heads and MLP
+columns split as models/clef/weights.py:60-67), o-proj and down-proj partial
+sums are all-reduced in FP32 over NCCL before the cast (qwen3_5/pallas.py:
+66-69,121), and rank 0's logits must match the single-GPU oracle.
+
+Runs one spawned process per GPU; skipped with fewer than two GPUs.
+"""
+
+from __future__ import annotations
+
+import multiprocessing as mp
+import traceback
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, nccl_id, dtype, queue):
+    try:
+        import sys
+        from pathlib import Path
+
+        root = Path(__file__).resolve().parents[1]
+        sys.path[:0] = [str(root), str(root / "tests")]
+        from gpu_helpers import round_tree
+
+        from deciax_b200.config import HeadConfig, TextConfig
+        from deciax_b200.model import ClefCudaModel
+        from deciax_b200.synthetic import BatchSpec, synthetic_batch, synthetic_weights
+
+        config = TextConfig.full_attention(hidden_size=512, intermediate_size=1024, num_attention_heads=4,
+                                           num_key_value_heads=2, head_dim=256, num_layers=2, vocab_size=300)
+        head = HeadConfig(heads=4, routing_layers=1, layers=1, width=64, ffn=128)
+        top, layers, hp = synthetic_weights(config, head, seed=5, embed_std=1.0)
+        top, layers, hp = round_tree(top, dtype), round_tree(layers, dtype), round_tree(hp, dtype)
+        model = ClefCudaModel.from_arrays(config, head, top, layers, hp, dtype=dtype, device=rank, tp_rank=rank,
+                                          tp_size=world, nccl_id=nccl_id, max_seq_len=256)
+        arrays = synthetic_batch(BatchSpec(states=3, seq=256, questions=2, options_per_question=3,
+                                           lengths=(256, 130, 40), row_bucket=4), config.vocab_size, seed=6)
+        logits, hidden = model.forward_with_hidden(arrays)
+        queue.put((rank, logits, hidden, None))
+        model.close()
+    except Exception:  # report instead of hanging the parent
+        queue.put((rank, None, None, traceback.format_exc()))
+
+
+def _run_tp(world: int, dtype: str):
+    import torch
+
+    from deciax_b200 import _lib
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import ctypes
+
+    lib = _lib.load()
+    nid = ctypes.create_string_buffer(_lib.NCCL_ID_BYTES)
+    _lib.check(lib.clef_nccl_unique_id(nid))
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, nid.raw, dtype, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            rank, logits, hidden, err = queue.get(timeout=600)
+            assert err is None, err
+            results[rank] = (logits, hidden)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():  # a peer that died leaves the other blocked in NCCL init
+                p.terminate()
+    return results
+
+
+def _oracle(dtype):
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from gpu_helpers import oracle_config, oracle_head, round_tree
+
+    from deciax_b200.config import HeadConfig, TextConfig
+    from deciax_b200.synthetic import BatchSpec, synthetic_batch, synthetic_weights
+    from oracle import clef_oracle as O
+
+    config = TextConfig.full_attention(hidden_size=512, intermediate_size=1024, num_attention_heads=4,
+                                       num_key_value_heads=2, head_dim=256, num_layers=2, vocab_size=300)
+    head = HeadConfig(heads=4, routing_layers=1, layers=1, width=64, ffn=128)
+    top, layers, hp = synthetic_weights(config, head, seed=5, embed_std=1.0)
+    top, layers, hp = round_tree(top, dtype), round_tree(layers, dtype), round_tree(hp, dtype)
+    arrays = synthetic_batch(BatchSpec(states=3, seq=256, questions=2, options_per_question=3,
+                                       lengths=(256, 130, 40), row_bucket=4), config.vocab_size, seed=6)
+    logits, hidden = O.forward(top, layers, hp, arrays, oracle_config(config), oracle_head(head), dtype, return_hidden=True)
+    return arrays, logits, hidden
+
+
+def test_tp2_fp32_matches_oracle():
+    results = _run_tp(2, "fp32")
+    arrays, exp_logits, exp_hidden = _oracle("fp32")
+    valid = arrays["mask"]
+    scale = np.abs(exp_hidden[valid]).max()
+    for rank, (logits, hidden) in results.items():
+        np.testing.assert_allclose(hidden[valid], exp_hidden[valid], rtol=1e-4, atol=1e-4 * scale)
+        m = arrays["option_mask"]
+        np.testing.assert_allclose(logits[m], exp_logits[m], rtol=1e-4, atol=1e-4)
+    np.testing.assert_array_equal(results[0][0], results[1][0])  # every rank ends with the same logits
+
+
+def test_tp2_bf16_probabilities():
+    from gpu_helpers import probs_close
+
+    results = _run_tp(2, "bf16")
+    arrays, exp_logits, _ = _oracle("bf16")
+    err, flips = probs_close(results[0][0], exp_logits, arrays)
+    assert err < 1e-2 and flips == 0, (err, flips)
