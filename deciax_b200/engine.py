@@ -1,0 +1,132 @@
+"""``ClefEngine``: answers a batch of states against one question schema.
+
+Mirrors ``src/deciax/runtime/clef.py:18-40`` (same constructor argument,
+``decide_batch`` signature, results in input order, the same ``ValueError``
+for ``head_max_len``) with three changes to how the work is scheduled; none
+changes a record's answer, because a record's logits do not depend on the
+other rows or the padding of its batch:
+
+* the schema is tokenised once per call and the states as one tokenizer batch
+  (``SchemaPrompt.encode_states``) instead of one full ``encode`` per state;
+* records are grouped by length into batches whose padded size
+  (rows x sequence bucket) stays within ``max_batch_tokens``, with row counts
+  that fill a row bucket exactly, instead of fixed pairs in input order;
+* batches go to every replica at once (data parallelism: one model per GPU,
+  each with full weights, no collective), one host thread per replica.  The
+  library releases the GIL for the whole forward, so replicas run
+  concurrently; while a replica computes, its thread's next batch is already
+  collated by a helper thread.
+
+A replica is anything with ``forward(arrays) -> [b, o] logits``, ``name``,
+``tokenizer``, ``pad_token_id`` and ``max_token_budget`` (``ClefCudaModel``).
+Each replica serves one batch at a time (``forward`` is not re-entrant per
+handle); ``decide_batch`` calls may come from several threads.
+"""
+
+from __future__ import annotations
+
+import queue
+import threading
+from collections.abc import Mapping, Sequence
+from concurrent.futures import ThreadPoolExecutor
+from typing import Any
+
+import numpy as np
+
+from deciax_b200.clef_input import ROW_BUCKETS, SEQUENCE_BUCKETS, Record, SchemaPrompt, bucket, collate, decode
+
+DEFAULT_BATCH_TOKENS = 65536
+
+
+def plan_batches(lengths: Sequence[int], max_batch_tokens: int = DEFAULT_BATCH_TOKENS,
+                 max_rows: int = ROW_BUCKETS[-1]) -> list[list[int]]:
+    """Group record indices into batches, longest first.
+
+    Each batch holds records of similar length; its row count is a row bucket
+    (no padded rows) unless fewer records remain, and rows x the sequence
+    bucket of its longest record stays within ``max_batch_tokens`` (a single
+    record longer than the budget gets a batch of its own).
+    """
+    order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
+    batches: list[list[int]] = []
+    pos = 0
+    while pos < len(order):
+        seq = bucket(lengths[order[pos]], SEQUENCE_BUCKETS)
+        cap = max(1, min(max_rows, max_batch_tokens // seq))
+        limit = min(cap, len(order) - pos)
+        rows = max(r for r in ROW_BUCKETS if r <= limit)
+        batches.append(order[pos : pos + rows])
+        pos += rows
+    return batches
+
+
+class ClefEngine:
+    def __init__(self, model: Any, *, replicas: Sequence[Any] | None = None,
+                 max_batch_tokens: int = DEFAULT_BATCH_TOKENS) -> None:
+        self.model = model
+        self.replicas = list(replicas) if replicas else [model]
+        if max_batch_tokens < 1:
+            raise ValueError("max_batch_tokens must be positive")
+        self.max_batch_tokens = max_batch_tokens
+        self._locks = [threading.Lock() for _ in self.replicas]
+
+    def encode(self, states: Sequence[Any], questions: Mapping[Any, Mapping[str, Any]], max_len: int | None) -> list[Record]:
+        model = self.model
+        prompt = SchemaPrompt(model.tokenizer, questions)
+        return prompt.encode_states(list(states), model.max_token_budget if max_len is None else max_len)
+
+    def decide_batch(self, states: Sequence[Any], questions: Mapping[Any, Mapping[str, Any]], *, max_len: int | None = None,
+                     head_max_len: int | None = None) -> list[dict[str, Any]]:
+        if head_max_len is not None:
+            raise ValueError("Clef has one joint token budget; head_max_len is unsupported")
+        records = self.encode(states, questions, max_len)
+        if not records:
+            return []
+        batches = plan_batches([len(r.ids) for r in records], self.max_batch_tokens)
+        results: list[dict[str, Any] | None] = [None] * len(records)
+        work: queue.Queue[list[int]] = queue.Queue()
+        for b in batches:
+            work.put(b)
+        errors: list[BaseException] = []
+        pad_id, name = self.model.pad_token_id, self.model.name
+
+        def prepare(idx: list[int]) -> tuple[list[int], dict[str, np.ndarray]]:
+            return idx, collate([records[i] for i in idx], pad_id)
+
+        def serve(k: int) -> None:
+            replica, lock = self.replicas[k], self._locks[k]
+            with ThreadPoolExecutor(1) as helper:
+                pending = None
+                while not errors:
+                    if pending is None:
+                        try:
+                            pending = helper.submit(prepare, work.get_nowait())
+                        except queue.Empty:
+                            return
+                    idx, arrays = pending.result()
+                    try:
+                        pending = helper.submit(prepare, work.get_nowait())
+                    except queue.Empty:
+                        pending = None
+                    with lock:
+                        logits = np.asarray(replica.forward(arrays), np.float32)
+                    for row, i in enumerate(idx):
+                        results[i] = decode(records[i], logits[row], questions, name)
+
+        def guarded(k: int) -> None:
+            try:
+                serve(k)
+            except BaseException as e:  # re-raised in the caller's thread
+                errors.append(e)
+
+        if len(self.replicas) == 1 or len(batches) == 1:
+            serve(0)
+        else:
+            threads = [threading.Thread(target=guarded, args=(k,), daemon=True) for k in range(len(self.replicas))]
+            for t in threads:
+                t.start()
+            for t in threads:
+                t.join()
+            if errors:
+                raise errors[0]
+        return results  # type: ignore[return-value]

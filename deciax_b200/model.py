@@ -20,9 +20,8 @@ import ml_dtypes
 import numpy as np
 
 from deciax_b200 import _lib
+from deciax_b200.clef_input import MAX_TOKENS, SEQUENCE_BUCKETS
 from deciax_b200.config import HeadConfig, KernelFlags, TextConfig
-
-MAX_TOKENS = 16384  # models/clef/input.py:25-26
 
 INT_KEYS = ("input_ids", "lexical_ids", "lexical_spans", "question_spans", "types", "option_spans", "option_field")
 BOOL_KEYS = ("mask", "question_mask", "option_mask")
@@ -93,6 +92,9 @@ class ClefCudaModel:
         self.device = device
         self.tokenizer = tokenizer
         self.pad_token_id = pad_token_id
+        # records are encoded so that their sequence bucket fits the library's max_seq_len
+        fits = [b for b in SEQUENCE_BUCKETS if b <= max_seq_len]
+        self.max_token_budget = fits[-1] if fits else max_seq_len
         self._lib = _lib.load()
         n = len(config.layer_types)
         self._types = (ctypes.c_int32 * n)(*[_lib.LAYER_LINEAR if t == "linear_attention" else _lib.LAYER_FULL for t in config.layer_types])

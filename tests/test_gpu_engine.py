@@ -1,0 +1,79 @@
+"""``ClefEngine`` over ``ClefCudaModel`` replicas: length-grouped batches and
+data-parallel replicas give the answers of one-record forwards (the
+reference's ``decide_batch`` semantics, ``runtime/clef.py:23-40``)."""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+from conftest import GOLDEN
+from gpu_helpers import round_tree
+from tokenizers import Tokenizer
+
+from deciax_b200 import clef_input as I
+from deciax_b200.config import HeadConfig, TextConfig
+from deciax_b200.engine import ClefEngine
+from deciax_b200.model import ClefCudaModel
+from deciax_b200.synthetic import synthetic_weights
+
+pytestmark = pytest.mark.gpu
+
+FIX = json.loads((GOLDEN / "clef_input.json").read_text())
+TOK = Tokenizer.from_str(FIX["tokenizer"])
+PAD = TOK.token_to_id("<|endoftext|>")
+CONFIG = TextConfig.full_attention(hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2,
+                                   head_dim=64, num_layers=2, vocab_size=512)
+HEAD = HeadConfig(heads=4, routing_layers=2, layers=2, width=64, ffn=128)
+
+
+def replica(device: int):
+    top, layers, hp = (round_tree(t, "bf16") for t in synthetic_weights(CONFIG, HEAD, 3, embed_std=1.0))
+    return ClefCudaModel.from_arrays(CONFIG, HEAD, top, layers, hp, dtype="bf16", device=device, max_seq_len=2048,
+                                     tokenizer=TOK, pad_token_id=PAD)
+
+
+def states(n: int) -> list[str]:
+    rng = np.random.default_rng(5)
+    words = ["hello", "world", "ticket", "Printer", "jammed", "urgent", "floor", "priority"]
+    return [" ".join(rng.choice(words, size=int(rng.integers(1, 700)))) for _ in range(n)] + FIX["states"]
+
+
+def close(a, b, tol=2e-3) -> bool:
+    if isinstance(a, dict):
+        return a.keys() == b.keys() and all(close(a[k], b[k], tol) for k in a)
+    if isinstance(a, float):
+        return abs(a - b) <= tol
+    return a == b
+
+
+def one_by_one(model, ss, questions):
+    out = []
+    for s in ss:
+        r = I.encode(TOK, s, questions, model.max_token_budget)
+        out.append(I.decode(r, model.forward(I.collate([r], PAD))[0], questions, model.name))
+    return out
+
+
+def test_engine_batches_match_single_record_forwards():
+    model = replica(0)
+    questions = FIX["schemas"]["mixed"]
+    ss = states(21)
+    got = model.build_engine().decide_batch(ss, questions)
+    want = one_by_one(model, ss, questions)
+    assert all(close(g, w) for g, w in zip(got, want, strict=True))
+
+
+def test_engine_data_parallel_over_gpus():
+    import torch
+
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    replicas = [replica(d) for d in range(min(n, 4))]
+    questions = FIX["schemas"]["reference_test"]
+    ss = states(40)
+    got = ClefEngine(replicas[0], replicas=replicas, max_batch_tokens=4096).decide_batch(ss, questions)
+    want = one_by_one(replicas[0], ss, questions)
+    assert all(close(g, w) for g, w in zip(got, want, strict=True))
