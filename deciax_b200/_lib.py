@@ -39,6 +39,7 @@ EXPORTS = (
     "clef_op_qk_norm_rope",
     "clef_op_qk_norm_rope_noalloc",
     "clef_op_attention",
+    "clef_op_gdn_core",
 )
 
 
@@ -64,6 +65,11 @@ class ClefConfigC(ctypes.Structure):
         ("attn_softcap", ctypes.c_float),
         ("layer_window", ctypes.POINTER(ctypes.c_int32)),
         ("embed_scale", ctypes.c_float),
+        ("linear_num_key_heads", ctypes.c_int32),
+        ("linear_num_value_heads", ctypes.c_int32),
+        ("linear_key_head_dim", ctypes.c_int32),
+        ("linear_value_head_dim", ctypes.c_int32),
+        ("linear_conv_kernel_dim", ctypes.c_int32),
     ]
 
 
@@ -140,6 +146,7 @@ def load() -> ctypes.CDLL:
             "clef_op_qk_norm_rope": [i32, vp, i32, i32, i32, i32, i32, f32, f32, vp, vp, f32, vp],
             "clef_op_qk_norm_rope_noalloc": [i32, vp, i32, i32, i32, i32, i32, f32, f32, vp, vp, f32, vp],
             "clef_op_attention": [i32, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, vp],
+            "clef_op_gdn_core": [i32, vp, i32, vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp],
         }
         for name, args in sigs.items():
             fn = getattr(lib, name)

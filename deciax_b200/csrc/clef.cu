@@ -6,8 +6,9 @@
 // -> joint head) on one CUDA stream, NCCL all-reduce for TP > 1, and the
 // C-ABI entry points declared in include/clef_b200.h.
 //
-// Device side: gemm_sm100.cuh (tcgen05 GEMM), attention.cuh, simt.cuh,
-// head.cuh.
+// Device side: gemm_sm100.cuh / gemm2_sm100.cuh (tcgen05 GEMMs),
+// attention_sm100.cuh (tcgen05 attention), attention.cuh, gdn.cuh (Gated
+// DeltaNet), simt.cuh, head.cuh.
 //
 // Reference: src/deciax/models/clef/model.py:30-102 (forward loop),
 // models/qwen3_5/text.py:94-102 (layer), models/qwen3_5/pallas.py:62-129 (TP
@@ -35,6 +36,7 @@
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm2_sm100.cuh"
+#include "gdn.cuh"
 #include "head.cuh"
 #include "simt.cuh"
 
@@ -162,7 +164,8 @@ enum Category : int {
   kCatResidual = 9,
   kCatHead = 10,
   kCatOther = 11,
-  kNumCategories = 12,
+  kCatGdn = 12,
+  kNumCategories = 13,
 };
 
 // Optional CUDA-event timeline: one event after every launch on the stream,
@@ -363,11 +366,39 @@ static void gemm_simt(Launcher& L, int epi, const T* A, int lda, const T* B, int
 }
 
 template <typename T>
-static void rmsnorm(Launcher& L, const T* x, int ldx, const T* w, T* out, int ldo, int rows, int dim, float eps) {
+static void rmsnorm(Launcher& L, const T* x, int ldx, const T* w, T* out, int ldo, int rows, int dim, float eps,
+                    const uint8_t* row_mask = nullptr) {
   const int warps = 8;
-  rmsnorm_kernel<T><<<(rows + warps - 1) / warps, warps * 32, 0, L.stream>>>(x, ldx, w, out, ldo, rows, dim, eps);
+  rmsnorm_kernel<T><<<(rows + warps - 1) / warps, warps * 32, 0, L.stream>>>(x, ldx, w, out, ldo, rows, dim, eps,
+                                                                            row_mask);
   CUDA_CHECK(cudaGetLastError());
   L.tick();
+}
+
+template <typename T, int DH>
+static void launch_gdn_dh(Launcher& L, const GdnArgs& a) {
+  const size_t smem = GdnShape<DH>::bytes;
+  CUDA_CHECK(cudaFuncSetAttribute(gdn_chunk_kernel<T, DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem)));
+  gdn_chunk_kernel<T, DH><<<dim3(a.nv, a.B), kGdnThreads, smem, L.stream>>>(a);
+  CUDA_CHECK(cudaGetLastError());
+  L.tick();
+}
+
+// One CTA per (state, value head); the head dim is a template parameter.
+template <typename T>
+static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
+  REQUIRE(a.B > 0 && a.S > 0 && a.nh > 0 && a.nv > 0 && a.nv % a.nh == 0, "bad Gated DeltaNet shape");
+  REQUIRE(a.width >= 1 && a.width <= 8, "linear_conv_kernel_dim must be 1..8");
+  REQUIRE(a.B <= 65535, "too many states");
+  switch (dh) {
+    case 8: launch_gdn_dh<T, 8>(L, a); break;
+    case 16: launch_gdn_dh<T, 16>(L, a); break;
+    case 32: launch_gdn_dh<T, 32>(L, a); break;
+    case 64: launch_gdn_dh<T, 64>(L, a); break;
+    case 128: launch_gdn_dh<T, 128>(L, a); break;
+    default: throw Error(CLEF_EINVAL, "Gated DeltaNet head dim must be one of 8, 16, 32, 64, 128");
+  }
 }
 
 template <typename T>
@@ -560,6 +591,12 @@ struct Layer {
   DBuf w_o;     // [D, Hq_l*d]
   DBuf w_gu;    // [2*Fp, D]: 256-row blocks of [128 gate rows | 128 up rows]
   DBuf w_down;  // [D, Fp]
+  // linear_attention (Gated DeltaNet) layers
+  DBuf g_proj;     // [Ng_pad, D]: q (nh_l*dh), k (nh_l*dh), v (nv_l*dh), z (nv_l*dh), a (nv_l), b (nv_l) rows, zero pad
+  DBuf g_conv;     // [Cg, width]: q, k, v conv rows (projection column order)
+  DBuf g_alog, g_dtb;  // [nv_l]
+  DBuf g_norm;     // [dh]
+  DBuf g_out;      // [D, nv_l*dh]
   std::set<std::string> have;
 };
 
@@ -570,7 +607,7 @@ struct Layer {
 struct Workspace {
   int b = 0, s = 0, lx = 0, o = 0, q = 0;
   DBuf ints, bytes;  // staged batch arrays (device)
-  DBuf x, h, qkv, attn, gu, act, partial;
+  DBuf x, h, qkv, attn, gu, act, partial, gproj;
   DBuf memory, mnorm, kv;
   DBuf gv, questions, contexts, lexical;
   DBuf small;  // head buffers of size b*max(o,q)*max(W,FF,4W)
@@ -587,6 +624,9 @@ struct Model {
   int D = 0, F = 0, Hq = 0, Hkv = 0, d = 0, L = 0, V = 0;
   int Hq_l = 0, Hkv_l = 0, F_l = 0, Fp = 0, Nqkv = 0, rot = 0;
   int W = 0, HH = 0, RL = 0, HL = 0, FF = 0;
+  // Gated DeltaNet dims (global / this rank) and packed projection layout
+  int g_nh = 0, g_nv = 0, g_dh = 0, g_width = 0, g_nh_l = 0, g_nv_l = 0, Ng = 0, Ng_pad = 0, Cg = 0;
+  bool any_linear = false;
   bool finalized = false;
   std::string last_error;
   cudaStream_t stream = nullptr;
@@ -666,8 +706,6 @@ struct Model {
       if (c.layer_window) layer_window[i] = c.layer_window[i];
       REQUIRE(layer_types[i] == CLEF_LAYER_FULL_ATTENTION || layer_types[i] == CLEF_LAYER_LINEAR_ATTENTION,
               "unsupported Qwen3.5 layer types");
-      REQUIRE(layer_types[i] == CLEF_LAYER_FULL_ATTENTION,
-              "linear_attention (Gated DeltaNet) layers are not implemented by the CUDA library yet");
       REQUIRE(layer_window[i] >= 0, "window must be >= 0");
     }
     cfg.layer_types = nullptr;
@@ -680,6 +718,26 @@ struct Model {
     F_l = F / tp;
     Fp = (F_l + 127) / 128 * 128;
     Nqkv = Hq_l * 2 * d + 2 * Hkv_l * d;
+    for (int i = 0; i < L; ++i) any_linear |= layer_types[i] == CLEF_LAYER_LINEAR_ATTENTION;
+    if (any_linear) {
+      g_nh = c.linear_num_key_heads;
+      g_nv = c.linear_num_value_heads;
+      g_dh = c.linear_key_head_dim;
+      g_width = c.linear_conv_kernel_dim;
+      REQUIRE(g_nh > 0 && g_nv > 0 && g_dh > 0 && c.linear_value_head_dim > 0 && g_width > 0,
+              "Qwen3.5 dimensions must be positive");
+      REQUIRE(g_nv % g_nh == 0, "Qwen3.5 query/value heads must divide into key head groups");
+      REQUIRE(c.linear_value_head_dim == g_dh && (g_dh == 8 || g_dh == 16 || g_dh == 32 || g_dh == 64 || g_dh == 128),
+              "Gated DeltaNet needs linear_key_head_dim == linear_value_head_dim in {8, 16, 32, 64, 128}");
+      REQUIRE(g_width <= 8, "linear_conv_kernel_dim must be at most 8");
+      // heads shard evenly across TP ranks (qwen3_5/pallas.py:84-90)
+      REQUIRE(g_nh % tp == 0 && g_nv % tp == 0, "linear attention heads must divide by tp");
+      g_nh_l = g_nh / tp;
+      g_nv_l = g_nv / tp;
+      Cg = 2 * g_nh_l * g_dh + g_nv_l * g_dh;
+      Ng = Cg + g_nv_l * g_dh + 2 * g_nv_l;
+      Ng_pad = (Ng + 15) / 16 * 16;
+    }
 
     CUDA_CHECK(cudaSetDevice(device));
     CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
@@ -695,13 +753,24 @@ struct Model {
     lm_head.alloc(static_cast<size_t>(V) * D * esz);
     final_norm.alloc(static_cast<size_t>(D) * esz);
     layers.resize(L);
-    for (auto& l : layers) {
+    for (int li = 0; li < L; ++li) {
+      Layer& l = layers[li];
       l.w_in.alloc(static_cast<size_t>(D) * esz);
       l.w_post.alloc(static_cast<size_t>(D) * esz);
-      l.q_norm.alloc(static_cast<size_t>(d) * esz);
-      l.k_norm.alloc(static_cast<size_t>(d) * esz);
-      l.w_qkv.alloc(static_cast<size_t>(Nqkv) * D * esz);
-      l.w_o.alloc(static_cast<size_t>(D) * Hq_l * d * esz);
+      if (layer_types[li] == CLEF_LAYER_LINEAR_ATTENTION) {
+        l.g_proj.alloc(static_cast<size_t>(Ng_pad) * D * esz);
+        CUDA_CHECK(cudaMemset(l.g_proj.p, 0, l.g_proj.bytes));
+        l.g_conv.alloc(static_cast<size_t>(Cg) * g_width * esz);
+        l.g_alog.alloc(static_cast<size_t>(g_nv_l) * esz);
+        l.g_dtb.alloc(static_cast<size_t>(g_nv_l) * esz);
+        l.g_norm.alloc(static_cast<size_t>(g_dh) * esz);
+        l.g_out.alloc(static_cast<size_t>(D) * g_nv_l * g_dh * esz);
+      } else {
+        l.q_norm.alloc(static_cast<size_t>(d) * esz);
+        l.k_norm.alloc(static_cast<size_t>(d) * esz);
+        l.w_qkv.alloc(static_cast<size_t>(Nqkv) * D * esz);
+        l.w_o.alloc(static_cast<size_t>(D) * Hq_l * d * esz);
+      }
       l.w_gu.alloc(static_cast<size_t>(2) * Fp * D * esz);
       l.w_down.alloc(static_cast<size_t>(D) * Fp * esz);
       CUDA_CHECK(cudaMemset(l.w_gu.p, 0, l.w_gu.bytes));
@@ -783,6 +852,61 @@ struct Model {
     }
   }
 
+  // Gated DeltaNet tensors of one layer, sharded by heads (models/clef/weights.py:43-67):
+  // q/k rows by key heads, v/z/a/b rows and out_proj columns by value heads.
+  // Accepts the split names of weights.py:43-57 and the checkpoint's fused
+  // in_proj_qkv / conv1d tensors.
+  void upload_gdn(const std::string& name, const std::string& key, Layer& l, const void* host, int host_dtype,
+                  const int64_t* shape, int ndim) {
+    const int64_t dh = g_dh, nk = static_cast<int64_t>(g_nh) * dh, nk_l = static_cast<int64_t>(g_nh_l) * dh;
+    const int64_t nvd = static_cast<int64_t>(g_nv) * dh, nvd_l = static_cast<int64_t>(g_nv_l) * dh;
+    const int64_t z0 = Cg, a0 = Cg + nvd_l, b0 = a0 + g_nv_l;
+    // rows [src0 + rank*n, +n) of a [*, cols] host tensor into rows dst0.. of a packed device matrix
+    auto rows = [&](int64_t cols, int64_t src0, int64_t n, DBuf& dst, int64_t dst0) {
+      put_block(host, host_dtype, cols, src0 + rank * n, n, 0, cols, dst.p, dst0, cols);
+    };
+    if (key == "q.weight" || key == "k.weight") {
+      expect_shape(name, shape, ndim, {nk, D});
+      rows(D, 0, nk_l, l.g_proj, key[0] == 'q' ? 0 : nk_l);
+    } else if (key == "v.weight" || key == "in_proj_z.weight") {
+      expect_shape(name, shape, ndim, {nvd, D});
+      rows(D, 0, nvd_l, l.g_proj, key[0] == 'v' ? 2 * nk_l : z0);
+    } else if (key == "in_proj_a.weight" || key == "in_proj_b.weight") {
+      expect_shape(name, shape, ndim, {g_nv, D});
+      rows(D, 0, g_nv_l, l.g_proj, key[8] == 'a' ? a0 : b0);
+    } else if (key == "in_proj_qkv.weight") {
+      expect_shape(name, shape, ndim, {2 * nk + nvd, D});
+      rows(D, 0, nk_l, l.g_proj, 0);
+      rows(D, nk, nk_l, l.g_proj, nk_l);
+      rows(D, 2 * nk, nvd_l, l.g_proj, 2 * nk_l);
+      for (const char* k : {"q.weight", "k.weight", "v.weight"}) l.have.insert(std::string("mixer.") + k);
+    } else if (key == "q.conv" || key == "k.conv") {
+      expect_shape(name, shape, ndim, {nk, g_width});
+      rows(g_width, 0, nk_l, l.g_conv, key[0] == 'q' ? 0 : nk_l);
+    } else if (key == "v.conv") {
+      expect_shape(name, shape, ndim, {nvd, g_width});
+      rows(g_width, 0, nvd_l, l.g_conv, 2 * nk_l);
+    } else if (key == "conv1d.weight") {
+      expect_shape(name, shape, ndim, {2 * nk + nvd, 1, g_width});
+      rows(g_width, 0, nk_l, l.g_conv, 0);
+      rows(g_width, nk, nk_l, l.g_conv, nk_l);
+      rows(g_width, 2 * nk, nvd_l, l.g_conv, 2 * nk_l);
+      for (const char* k : {"q.conv", "k.conv", "v.conv"}) l.have.insert(std::string("mixer.") + k);
+    } else if (key == "A_log" || key == "dt_bias") {
+      expect_shape(name, shape, ndim, {g_nv});
+      put_block(host, host_dtype, g_nv, 0, 1, static_cast<int64_t>(rank) * g_nv_l, g_nv_l,
+                (key[0] == 'A' ? l.g_alog : l.g_dtb).p, 0, g_nv_l);
+    } else if (key == "norm.weight") {
+      expect_shape(name, shape, ndim, {dh});
+      put_block(host, host_dtype, dh, 0, 1, 0, dh, l.g_norm.p, 0, dh);
+    } else if (key == "out_proj.weight") {
+      expect_shape(name, shape, ndim, {D, nvd});
+      put_block(host, host_dtype, nvd, 0, D, rank * nvd_l, nvd_l, l.g_out.p, 0, nvd_l);
+    } else {
+      throw Error(CLEF_EINVAL, "unexpected backbone tensor: " + name);
+    }
+  }
+
   void upload(const std::string& name, const void* host, int host_dtype, const int64_t* shape, int ndim) {
     REQUIRE(!finalized, "clef_upload after clef_finalize");
     REQUIRE(host != nullptr, "null host pointer");
@@ -824,6 +948,11 @@ struct Model {
       const std::string key = name.substr(dot + 1);
       Layer& l = layers[li];
       const int64_t qrows = static_cast<int64_t>(Hq_l) * 2 * d, krows = static_cast<int64_t>(Hkv_l) * d;
+      if (layer_types[li] == CLEF_LAYER_LINEAR_ATTENTION && key.rfind("mixer.", 0) == 0) {
+        upload_gdn(name, key.substr(6), l, host, host_dtype, shape, ndim);
+        l.have.insert(key);
+        return;
+      }
       if (key == "input_layernorm.weight" || key == "post_attention_layernorm.weight") {
         expect_shape(name, shape, ndim, {D});
         put_block(host, host_dtype, D, 0, 1, 0, D, (key[0] == 'i' ? l.w_in : l.w_post).p, 0, D);
@@ -888,9 +1017,21 @@ struct Model {
                           "mixer.k_norm.weight",    "mixer.q_proj.weight",            "mixer.k_proj.weight",
                           "mixer.v_proj.weight",    "mixer.o_proj.weight",            "mlp.gate_proj.weight",
                           "mlp.up_proj.weight",     "mlp.down_proj.weight"};
-    for (int i = 0; i < L; ++i)
-      for (const char* k : keys)
-        REQUIRE(layers[i].have.count(k), "incomplete Clef text checkpoint: layers." + std::to_string(i) + "." + k);
+    const char* gdn_keys[] = {"input_layernorm.weight", "post_attention_layernorm.weight", "mixer.q.weight",
+                              "mixer.k.weight",         "mixer.v.weight",                  "mixer.in_proj_z.weight",
+                              "mixer.in_proj_a.weight", "mixer.in_proj_b.weight",          "mixer.q.conv",
+                              "mixer.k.conv",           "mixer.v.conv",                    "mixer.A_log",
+                              "mixer.dt_bias",          "mixer.norm.weight",               "mixer.out_proj.weight",
+                              "mlp.gate_proj.weight",   "mlp.up_proj.weight",              "mlp.down_proj.weight"};
+    for (int i = 0; i < L; ++i) {
+      if (layer_types[i] == CLEF_LAYER_LINEAR_ATTENTION) {
+        for (const char* k : gdn_keys)
+          REQUIRE(layers[i].have.count(k), "incomplete Clef text checkpoint: layers." + std::to_string(i) + "." + k);
+      } else {
+        for (const char* k : keys)
+          REQUIRE(layers[i].have.count(k), "incomplete Clef text checkpoint: layers." + std::to_string(i) + "." + k);
+      }
+    }
     auto ln = [&](const std::string& n, int64_t dim) {
       head_shape(n + ".weight", {dim});
       head_shape(n + ".bias", {dim});
@@ -966,7 +1107,8 @@ struct Model {
     w.x.ensure(act_bytes(T * D));
     w.h.ensure(act_bytes(T * D));
     w.qkv.ensure(act_bytes(T * Nqkv));
-    w.attn.ensure(act_bytes(T * Hq_l * d));
+    w.attn.ensure(act_bytes(T * std::max(Hq_l * d, g_nv_l * g_dh)));
+    if (any_linear) w.gproj.ensure(act_bytes(T * Ng_pad));
     if (dtype == CLEF_DTYPE_F32) w.gu.ensure(act_bytes(T * 2 * Fp));
     w.act.ensure(act_bytes(T * Fp));
     if (tp > 1) w.partial.ensure(T * D * 4);
@@ -1080,6 +1222,119 @@ struct Model {
     const uint8_t *mask, *q_mask, *o_mask;
   };
 
+  // Full-attention mixer + residual: RMSNorm, QKV projection (fused q/k-norm,
+  // RoPE and gate sigmoid where possible), causal GQA attention with the output
+  // gate, o-proj with the residual (text.py:70-98).
+  template <typename T>
+  void attention_mixer(Launcher& Lc, Layer& l, int li, const DevBatch& bt, T* x, T* hbuf, T* qkv, T* attn_out, int Tt) {
+    const int B = bt.b, S = bt.s;
+    const float eps = cfg.rms_norm_eps;
+    const int ldqkv = Nqkv;
+    cudaStream_t st = Lc.stream;
+    Lc.cat = kCatNorm;
+    rmsnorm<T>(Lc, x, D, l.w_in.as<T>(), hbuf, D, Tt, D, eps);
+    Lc.cat = kCatGemmQkv;
+    bool fused_qkv = false;
+    if constexpr (sizeof(T) == 2) {
+      if (qkv_fusable(d, rot)) {
+        const QkvFusion f{l.q_norm.as<bf16>(), l.k_norm.as<bf16>(), rope_cos.as<float>(), rope_sin.as<float>(),
+                          Hq_l,           Hkv_l,  d,  rot, S, eps};
+        gemm_bf16_qkv(Lc, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, f);
+        fused_qkv = true;
+      } else {
+        gemm_bf16(Lc, kEpiStore, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
+      }
+    } else {
+      gemm_simt<T>(Lc, kSimtStore, hbuf, D, l.w_qkv.as<T>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
+    }
+    if (!fused_qkv) {
+      const int warps = 8;
+      const long long items = static_cast<long long>(Tt) * (Hq_l + Hkv_l);
+      qk_norm_rope_kernel<T><<<static_cast<int>((items + warps - 1) / warps), warps * 32, warps * d * 4, st>>>(
+          qkv, ldqkv, Tt, S, Hq_l, Hkv_l, d, rot, l.q_norm.as<T>(), l.k_norm.as<T>(), rope_cos.as<float>(),
+          rope_sin.as<float>(), eps);
+      CUDA_CHECK(cudaGetLastError());
+      Lc.cat = kCatQkRope;
+      Lc.tick();
+    }
+    {
+      AttnArgs<T> a{};
+      a.q = qkv;
+      a.ldq = ldqkv;
+      a.hsq = 2 * d;
+      a.k = qkv + static_cast<size_t>(Hq_l) * 2 * d;
+      a.ldk = ldqkv;
+      a.hsk = d;
+      a.v = a.k + static_cast<size_t>(Hkv_l) * d;
+      a.ldv = ldqkv;
+      a.hsv = d;
+      a.gate = qkv + d;
+      a.ldg = ldqkv;
+      a.hsg = 2 * d;
+      a.out = attn_out;
+      a.ldo = static_cast<long long>(Hq_l) * d;
+      a.hso = d;
+      a.key_mask = bt.mask;
+      a.B = B;
+      a.Lq = S;
+      a.Lk = S;
+      a.H = Hq_l;
+      a.Hk = Hkv_l;
+      a.hd = d;
+      a.causal = 1;
+      a.softcap = cfg.attn_softcap;
+      a.window = layer_window[li];
+      a.status = Lc.status;
+      a.packed = 1;
+      a.gate_presig = fused_qkv ? 1 : 0;
+      Lc.cat = kCatAttention;
+      attention<T>(Lc, a);
+    }
+    Lc.cat = kCatGemmO;
+    project_residual<T>(Lc, attn_out, Hq_l * d, l.w_o.as<T>(), x, Tt);
+  }
+
+  // Gated DeltaNet mixer + residual (text.py:42-45,94-98): RMSNorm with padded
+  // rows zeroed, one packed projection GEMM [q|k|v|z|a|b], the fused
+  // conv/recurrence/gated-norm kernel, out_proj with the residual (FP32 TP sum
+  // before the cast when tp > 1).
+  template <typename T>
+  void gdn_mixer(Launcher& Lc, Layer& l, const DevBatch& bt, T* x, T* hbuf, T* core, int Tt) {
+    Lc.cat = kCatNorm;
+    rmsnorm<T>(Lc, x, D, l.w_in.as<T>(), hbuf, D, Tt, D, cfg.rms_norm_eps, bt.mask);
+    T* proj = ws.gproj.as<T>();
+    Lc.cat = kCatGemmQkv;
+    if constexpr (sizeof(T) == 2)
+      gemm_bf16(Lc, kEpiStore, hbuf, D, l.g_proj.as<bf16>(), D, Tt, Ng_pad, D, proj, Ng_pad, nullptr, nullptr, 0);
+    else
+      gemm_simt<T>(Lc, kSimtStore, hbuf, D, l.g_proj.as<T>(), D, Tt, Ng_pad, D, proj, Ng_pad, nullptr, nullptr, 0);
+    GdnArgs a{};
+    a.proj = proj;
+    a.ldp = Ng_pad;
+    a.k_col = g_nh_l * g_dh;
+    a.v_col = 2 * g_nh_l * g_dh;
+    a.z_col = Cg;
+    a.a_col = Cg + g_nv_l * g_dh;
+    a.b_col = a.a_col + g_nv_l;
+    a.conv = l.g_conv.p;
+    a.width = g_width;
+    a.A_log = l.g_alog.p;
+    a.dt_bias = l.g_dtb.p;
+    a.norm_w = l.g_norm.p;
+    a.out = core;
+    a.ldo = static_cast<long long>(g_nv_l) * g_dh;
+    a.B = bt.b;
+    a.S = bt.s;
+    a.nh = g_nh_l;
+    a.nv = g_nv_l;
+    a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(g_dh)));
+    a.eps = cfg.rms_norm_eps;
+    Lc.cat = kCatGdn;
+    launch_gdn<T>(Lc, a, g_dh);
+    Lc.cat = kCatGemmO;
+    project_residual<T>(Lc, core, g_nv_l * g_dh, l.g_out.as<T>(), x, Tt);
+  }
+
   template <typename T>
   void forward_impl(const DevBatch& bt, float* logits, cudaStream_t st) {
     REQUIRE(finalized, "clef_forward before clef_finalize");
@@ -1094,6 +1349,7 @@ struct Model {
     T* attn_out = w.attn.as<T>();
     T* act = w.act.as<T>();
     const float eps = cfg.rms_norm_eps;
+    (void)S;
 
     // 1. embedding (model.py:95)
     {
@@ -1105,70 +1361,12 @@ struct Model {
       Lc.tick();
     }
     // 2. decoder layers (text.py:94-102; TP: pallas.py:62-129)
-    const int ldqkv = Nqkv;
     for (int li = 0; li < L; ++li) {
       Layer& l = layers[li];
-      Lc.cat = kCatNorm;
-      rmsnorm<T>(Lc, x, D, l.w_in.as<T>(), hbuf, D, Tt, D, eps);
-      Lc.cat = kCatGemmQkv;
-      bool fused_qkv = false;
-      if constexpr (sizeof(T) == 2) {
-        if (qkv_fusable(d, rot)) {
-          const QkvFusion f{l.q_norm.as<bf16>(), l.k_norm.as<bf16>(), rope_cos.as<float>(), rope_sin.as<float>(),
-                            Hq_l,           Hkv_l,  d,  rot, S, eps};
-          gemm_bf16_qkv(Lc, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, f);
-          fused_qkv = true;
-        } else {
-          gemm_bf16(Lc, kEpiStore, hbuf, D, l.w_qkv.as<bf16>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
-        }
-      } else {
-        gemm_simt<T>(Lc, kSimtStore, hbuf, D, l.w_qkv.as<T>(), D, Tt, Nqkv, D, qkv, ldqkv, nullptr, nullptr, 0);
-      }
-      if (!fused_qkv) {
-        const int warps = 8;
-        const long long items = static_cast<long long>(Tt) * (Hq_l + Hkv_l);
-        qk_norm_rope_kernel<T><<<static_cast<int>((items + warps - 1) / warps), warps * 32, warps * d * 4, st>>>(
-            qkv, ldqkv, Tt, S, Hq_l, Hkv_l, d, rot, l.q_norm.as<T>(), l.k_norm.as<T>(), rope_cos.as<float>(),
-            rope_sin.as<float>(), eps);
-        CUDA_CHECK(cudaGetLastError());
-        Lc.cat = kCatQkRope;
-        Lc.tick();
-      }
-      {
-        AttnArgs<T> a{};
-        a.q = qkv;
-        a.ldq = ldqkv;
-        a.hsq = 2 * d;
-        a.k = qkv + static_cast<size_t>(Hq_l) * 2 * d;
-        a.ldk = ldqkv;
-        a.hsk = d;
-        a.v = a.k + static_cast<size_t>(Hkv_l) * d;
-        a.ldv = ldqkv;
-        a.hsv = d;
-        a.gate = qkv + d;
-        a.ldg = ldqkv;
-        a.hsg = 2 * d;
-        a.out = attn_out;
-        a.ldo = static_cast<long long>(Hq_l) * d;
-        a.hso = d;
-        a.key_mask = bt.mask;
-        a.B = B;
-        a.Lq = S;
-        a.Lk = S;
-        a.H = Hq_l;
-        a.Hk = Hkv_l;
-        a.hd = d;
-        a.causal = 1;
-        a.softcap = cfg.attn_softcap;
-        a.window = layer_window[li];
-        a.status = Lc.status;
-        a.packed = 1;
-        a.gate_presig = fused_qkv ? 1 : 0;
-        Lc.cat = kCatAttention;
-        attention<T>(Lc, a);
-      }
-      Lc.cat = kCatGemmO;
-      project_residual<T>(Lc, attn_out, Hq_l * d, l.w_o.as<T>(), x, Tt);
+      if (layer_types[li] == CLEF_LAYER_LINEAR_ATTENTION)
+        gdn_mixer<T>(Lc, l, bt, x, hbuf, attn_out, Tt);
+      else
+        attention_mixer<T>(Lc, l, li, bt, x, hbuf, qkv, attn_out, Tt);
       Lc.cat = kCatNorm;
       rmsnorm<T>(Lc, x, D, l.w_post.as<T>(), hbuf, D, Tt, D, eps);
       Lc.cat = kCatGemmGateUp;
@@ -1830,6 +2028,44 @@ int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out
       run(static_cast<const bf16*>(qkv));
     else
       run(static_cast<const float*>(qkv));
+  });
+}
+
+int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int width, const void* A_log,
+                     const void* dt_bias, const void* norm_w, void* out, int b, int s, int nh, int nv, int dh, float eps,
+                     void* stream) {
+  return guarded(nullptr, [&] {
+    REQUIRE(proj && conv && A_log && dt_bias && norm_w && out, "null Gated DeltaNet argument");
+    REQUIRE(dtype == CLEF_DTYPE_BF16 || dtype == CLEF_DTYPE_F32, "dtype must be CLEF_DTYPE_BF16 or CLEF_DTYPE_F32");
+    REQUIRE(nh > 0 && nv > 0 && dh > 0 && nv % nh == 0, "Gated DeltaNet value heads must divide into key head groups");
+    const long long need = 2LL * nh * dh + 2LL * nv * dh + 2LL * nv;
+    REQUIRE(ldp >= need, "ldp is smaller than the packed projection width");
+    clef::Launcher L{static_cast<cudaStream_t>(stream), nullptr, 0};
+    clef::GdnArgs a{};
+    a.proj = proj;
+    a.ldp = ldp;
+    a.k_col = nh * dh;
+    a.v_col = 2 * nh * dh;
+    a.z_col = a.v_col + nv * dh;
+    a.a_col = a.z_col + nv * dh;
+    a.b_col = a.a_col + nv;
+    a.conv = conv;
+    a.width = width;
+    a.A_log = A_log;
+    a.dt_bias = dt_bias;
+    a.norm_w = norm_w;
+    a.out = out;
+    a.ldo = static_cast<long long>(nv) * dh;
+    a.B = b;
+    a.S = s;
+    a.nh = nh;
+    a.nv = nv;
+    a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
+    a.eps = eps;
+    if (dtype == CLEF_DTYPE_BF16)
+      clef::launch_gdn<bf16>(L, a, dh);
+    else
+      clef::launch_gdn<float>(L, a, dh);
   });
 }
 

@@ -95,15 +95,21 @@ __global__ void __launch_bounds__(256) simt_gemm(SimtGemmArgs<T> a) {
 // row norms (one warp per row)
 // ---------------------------------------------------------------------------
 
-// RMSNorm scaling by (1 + w): qwen3_5/text.py:25-28.
+// RMSNorm scaling by (1 + w): qwen3_5/text.py:25-28.  With row_mask, rows
+// whose mask byte is 0 are written as zeros (the Gated DeltaNet input
+// x * mask of text.py:43).
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ w, T* __restrict__ out, int ldo,
-                               int rows, int dim, float eps) {
+                               int rows, int dim, float eps, const uint8_t* __restrict__ row_mask) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const T* xr = x + static_cast<size_t>(row) * ldx;
   T* orow = out + static_cast<size_t>(row) * ldo;
+  if (row_mask != nullptr && row_mask[row] == 0) {
+    for (int i = lane; i < dim; i += 32) orow[i] = from_f32<T>(0.f);
+    return;
+  }
   float ss = 0.f;
   if constexpr (sizeof(T) == 2) {
     if ((dim & 7) == 0) {

@@ -123,6 +123,11 @@ class ClefCudaModel:
             attn_softcap=flags.attn_softcap,
             layer_window=self._window,
             embed_scale=flags.embed_scale,
+            linear_num_key_heads=config.linear_num_key_heads,
+            linear_num_value_heads=config.linear_num_value_heads,
+            linear_key_head_dim=config.linear_key_head_dim,
+            linear_value_head_dim=config.linear_value_head_dim,
+            linear_conv_kernel_dim=config.linear_conv_kernel_dim,
         )
         handle = ctypes.c_void_p()
         dt = _lib.DTYPE_BF16 if dtype == "bf16" else _lib.DTYPE_F32
@@ -152,7 +157,7 @@ class ClefCudaModel:
         _lib.check(self._lib.clef_finalize(self._handle), self._handle)
 
     TIMING_CATEGORIES = ("embed", "rmsnorm", "gemm_qkv", "qk_norm_rope", "attention", "gemm_o", "gemm_gate_up", "gemm_down",
-                         "allreduce", "residual_add", "head", "other")
+                         "allreduce", "residual_add", "head", "other", "gdn")
 
     def set_timing(self, enable: bool) -> None:
         _lib.check(self._lib.clef_set_timing(self._handle, int(enable)), self._handle)

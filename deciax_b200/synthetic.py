@@ -49,7 +49,17 @@ def synthetic_weights(config: TextConfig, head: HeadConfig, seed: int, std: floa
     emb = n(V, D, s=embed_std)
     top = {"embedding": emb, "lm_head": emb.copy(), "norm": n(D)}
     layers = []
-    for _ in config.layer_types:
+    for kind in config.layer_types:
+        if kind == "linear_attention":
+            layers.append({
+                "input_layernorm.weight": n(D),
+                "post_attention_layernorm.weight": n(D),
+                **gdn_weights(rng, config, std, cast),
+                "mlp.gate_proj.weight": n(F, D),
+                "mlp.up_proj.weight": n(F, D),
+                "mlp.down_proj.weight": n(D, F),
+            })
+            continue
         layers.append(
             {
                 "input_layernorm.weight": n(D),
@@ -66,6 +76,37 @@ def synthetic_weights(config: TextConfig, head: HeadConfig, seed: int, std: floa
             }
         )
     return top, layers, _head_weights(rng, D, head, std, cast)
+
+
+def gdn_weights(rng, config: TextConfig, std: float, cast) -> dict:
+    """Gated DeltaNet mixer weights under the split names of
+    models/clef/weights.py:43-57.  Projections N(0, std); conv taps N(0, 0.5)
+    (the scale of PyTorch's default Conv1d init at width 4); A_log = log of
+    U(0.01, 0.3), so per-token decays span slow and fast; dt_bias N(0, 0.5);
+    the gated norm's weight (applied as w, not 1 + w) 1 + N(0, 0.1)."""
+    D = config.hidden_size
+    nh, nv, dh, width = (config.linear_num_key_heads, config.linear_num_value_heads, config.linear_key_head_dim,
+                         config.linear_conv_kernel_dim)
+    dv = config.linear_value_head_dim
+
+    def n(*shape, s=std):
+        return cast(rng.standard_normal(shape, dtype=np.float32) * np.float32(s))
+
+    return {
+        "mixer.q.weight": n(nh * dh, D),
+        "mixer.k.weight": n(nh * dh, D),
+        "mixer.v.weight": n(nv * dv, D),
+        "mixer.in_proj_z.weight": n(nv * dv, D),
+        "mixer.in_proj_a.weight": n(nv, D),
+        "mixer.in_proj_b.weight": n(nv, D),
+        "mixer.q.conv": n(nh * dh, width, s=0.5),
+        "mixer.k.conv": n(nh * dh, width, s=0.5),
+        "mixer.v.conv": n(nv * dv, width, s=0.5),
+        "mixer.A_log": cast(np.log(rng.uniform(0.01, 0.3, nv)).astype(np.float32)),
+        "mixer.dt_bias": n(nv, s=0.5),
+        "mixer.norm.weight": cast((1 + rng.standard_normal(dv) * 0.1).astype(np.float32)),
+        "mixer.out_proj.weight": n(D, nv * dv),
+    }
 
 
 def synthetic_head_weights(hidden_size: int, head: HeadConfig, seed: int, std: float = 0.02, dtype: str = "fp32"):

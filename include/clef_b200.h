@@ -68,6 +68,13 @@ typedef struct ClefConfig {
   float attn_softcap;            /* softcap * tanh(score / softcap) on attention scores */
   const int32_t* layer_window;   /* [num_layers] causal window per layer, 0 = global; NULL = all global */
   float embed_scale;             /* multiply embeddings by this in the activation dtype */
+  /* Gated DeltaNet, the mixer of linear_attention layers (models/qwen3_5/text.py:42-67,
+   * config.py:15-19); read only when some layer is linear. */
+  int32_t linear_num_key_heads;
+  int32_t linear_num_value_heads;
+  int32_t linear_key_head_dim;   /* must equal linear_value_head_dim, one of 8, 16, 32, 64, 128 */
+  int32_t linear_value_head_dim;
+  int32_t linear_conv_kernel_dim; /* depthwise causal conv width, 1..8 */
 } ClefConfig;
 
 /* One collated batch: the dict returned by the reference collate()
@@ -104,7 +111,10 @@ int clef_create(const ClefConfig* config, int device, int tp_rank, int tp_size, 
  * library converts to the compute dtype, keeps this rank's shard and packs it.
  * Names: "embedding", "lm_head", "norm",
  *   "layers.{i}.{input_layernorm,post_attention_layernorm}.weight",
- *   "layers.{i}.mixer.{q_proj,k_proj,v_proj,o_proj,q_norm,k_norm}.weight",
+ *   "layers.{i}.mixer.{q_proj,k_proj,v_proj,o_proj,q_norm,k_norm}.weight" (full_attention),
+ *   "layers.{i}.mixer.{q,k,v,in_proj_z,in_proj_a,in_proj_b,out_proj,norm}.weight",
+ *   "layers.{i}.mixer.{q,k,v}.conv", "layers.{i}.mixer.{A_log,dt_bias}" (linear_attention:
+ *   the names after the in_proj_qkv / conv1d split of models/clef/weights.py:43-57),
  *   "layers.{i}.mlp.{gate_proj,up_proj,down_proj}.weight",
  *   "head.<joint_head.safetensors key>".
  * host_dtype: CLEF_DTYPE_F32 or CLEF_DTYPE_BF16 (raw bfloat16 bits). */
@@ -150,8 +160,9 @@ int clef_check_status(void* handle);
  * last report (then resets).  Categories: 0 embedding, 1 RMSNorm, 2 QKV GEMM,
  * 3 q/k-norm+RoPE, 4 attention, 5 o-proj GEMM, 6 gate/up GEMM, 7 down GEMM,
  * 8 NCCL all-reduce, 9 TP residual add, 10 lexical means + joint head,
- * 11 other. */
-#define CLEF_TIMING_CATEGORIES 12
+ * 11 other, 12 Gated DeltaNet core (linear_attention layers; their input
+ * projection counts as 2 and their output projection as 5). */
+#define CLEF_TIMING_CATEGORIES 13
 int clef_set_timing(void* handle, int enable);
 int clef_timing_report(void* handle, int n, float* ms, int* launches);
 
@@ -216,6 +227,18 @@ int clef_op_qk_norm_rope_noalloc(int dtype, void* qkv, int b, int s, int hq, int
  * (kernels/attention/blocked.py:9-32, text.py:90-91): out [b*s, Hq*d]. */
 int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out, int b, int s, int hq, int hkv, int d,
                       float softcap, int window, void* stream);
+
+/* Gated DeltaNet core, delta_net_core of models/qwen3_5/text.py:48-67 with the
+ * chunked rule of kernels/gdn/reference.py:40-92: from the projections
+ * proj [b*s, ldp] = [q (nh*dh) | k (nh*dh) | v (nv*dh) | z (nv*dh) | a (nv) | b (nv)]
+ * (the outputs of the q, k, v, in_proj_z, in_proj_a, in_proj_b dense layers, in
+ * that column order) to the gated, normalised output out [b*s, nv*dh] that
+ * feeds out_proj.  conv [2*nh*dh + nv*dh, width] holds the q, k and v conv
+ * rows; A_log, dt_bias [nv]; norm_w [dh].  dh = key = value head dim, one of
+ * 8, 16, 32, 64, 128; nv % nh == 0; width 1..8. */
+int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int width, const void* A_log,
+                     const void* dt_bias, const void* norm_w, void* out, int b, int s, int nh, int nv, int dh, float eps,
+                     void* stream);
 
 #ifdef __cplusplus
 }

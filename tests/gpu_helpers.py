@@ -39,6 +39,11 @@ def oracle_config(c: TextConfig, flags: KernelFlags = KernelFlags()) -> O.TextCo
         rms_norm_eps=c.rms_norm_eps,
         rope_theta=c.rope_theta,
         partial_rotary_factor=c.partial_rotary_factor,
+        linear_num_key_heads=c.linear_num_key_heads,
+        linear_num_value_heads=c.linear_num_value_heads,
+        linear_key_head_dim=c.linear_key_head_dim,
+        linear_value_head_dim=c.linear_value_head_dim,
+        linear_conv_kernel_dim=c.linear_conv_kernel_dim,
         attention=O.AttentionFlags(softcap=flags.attn_softcap, window=window),
     )
 
