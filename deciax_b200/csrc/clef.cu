@@ -1141,7 +1141,9 @@ struct Model {
     REQUIRE(static_cast<int>(w.shape[1]) == K, "dense(): inner dimension mismatch");
     const T* bp = bias ? bias->buf.as<T>() : nullptr;
     if constexpr (sizeof(T) == 2) {
-      if (!gelu && M >= 1024 && K % 8 == 0 && N % 8 == 0 && ldo % 8 == 0) {
+      // tcgen05 at every M: per-row results then do not depend on how many
+      // rows share the launch (answers are independent of batching).
+      if (!gelu && K % 8 == 0 && N % 8 == 0 && ldo % 8 == 0 && aligned16(x) && aligned16(w.buf.p) && aligned16(out)) {
         gemm_bf16(Lc, kEpiStore, x, K, w.buf.as<bf16>(), K, M, N, K, out, ldo, bp, nullptr, 0);
         return;
       }
@@ -1163,7 +1165,7 @@ struct Model {
     // q = T(query Wq^T + bq); [k|v] = T(memory [Wk;Wv]^T + [bk;bv])
     auto proj = [&](const T* x, int M, const T* w, int N, const T* b, T* o) {
       if constexpr (sizeof(T) == 2) {
-        if (M >= 1024 && W % 8 == 0) {
+        if (W % 8 == 0 && aligned16(x) && aligned16(w) && aligned16(o)) {
           gemm_bf16(Lc, kEpiStore, x, W, w, W, M, N, W, o, N, b, nullptr, 0);
           return;
         }

@@ -83,6 +83,28 @@ def test_gemm_bf16_tcgen05(m, n, k, epi):
     assert np.mean(got != expected) < 0.02  # almost every element bit-identical
 
 
+@pytest.mark.parametrize("n", [128, 768])
+def test_gemm_bf16_rows_do_not_depend_on_the_launch(n):
+    """A row's result is bit-identical whether it runs among 1000 rows (CTA
+    pairs for N >= 256), 300 rows or 64 rows (one CTA): the K order of the
+    tcgen05 accumulation does not depend on M, so batching cannot change an
+    answer."""
+    import torch
+
+    rng = np.random.default_rng(n)
+    k = 512
+    a = O.bf16(rng.standard_normal((1000, k)).astype(F32))
+    b = O.bf16(rng.standard_normal((n, k)).astype(F32) * F32(0.05))
+    A, B = dev(a, "bf16"), dev(b, "bf16")
+    full = torch.zeros((1000, n), dtype=torch.bfloat16, device="cuda")
+    run_gemm("bf16", 0, A, B, full, n)
+    for rows in (300, 64, 1):
+        part = torch.zeros((rows, n), dtype=torch.bfloat16, device="cuda")
+        sub = A[100 : 100 + rows].contiguous()
+        run_gemm("bf16", 0, sub, B, part, n)
+        assert torch.equal(part, full[100 : 100 + rows]), rows
+
+
 @pytest.mark.parametrize("m,f,k", [(128, 128, 64), (300, 256, 136), (1024, 1792, 512)])
 def test_gemm_bf16_swiglu_epilogue(m, f, k):
     import torch
