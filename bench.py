@@ -26,6 +26,7 @@ With torchrun (N > 1) every rank holds a full replica and runs its own batch
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -522,6 +523,78 @@ def attention_arm(args) -> None:
                       "dtype": "bf16", "data": "synthetic", "gpu_launches": args.steps}), flush=True)
 
 
+GDN = {"states": 8, "seq": 2048, "key_heads": 16, "value_heads": 32, "head_dim": 128, "conv": 4}
+
+
+def gdn_flops(c: dict) -> float:
+    """Algorithmic FLOPs of the chunked delta rule (64-token chunks) per
+    launch: per chunk and value head, k k^T and q k^T (2 C^2 dk each), the
+    triangular solve on dk + dv right-hand columns (C^2 (dk + dv)), X_k S,
+    (q e^g) S and the state update (2 C dk dv each), and (q k^T) value
+    (2 C^2 dv); the conv, norms and gates are O(C d) and not counted."""
+    C, dk, dv = 64, c["head_dim"], c["head_dim"]
+    per_chunk = 2 * C * C * dk * 2 + C * C * (dk + dv) + 3 * 2 * C * dk * dv + 2 * C * C * dv
+    chunks = -(-c["seq"] // C)
+    return float(per_chunk * chunks * c["value_heads"] * c["states"])
+
+
+def gdn_arm(args) -> None:
+    """The Gated DeltaNet core (conv, chunked delta rule, gated norm) of one
+    linear_attention layer, through clef_op_gdn_core at Qwen3.5-style dims
+    (16 key / 32 value heads of 128, conv 4) on 8 x 2048 tokens, BF16 I/O."""
+    import torch
+
+    from deciax_b200 import _lib
+    from deciax_b200.build import build as build_lib
+
+    build_lib()
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    c = GDN
+    B, S, nh, nv, dh = c["states"], c["seq"], c["key_heads"], c["value_heads"], c["head_dim"]
+    n = 2 * nh * dh + 2 * nv * dh + 2 * nv
+    gen = torch.Generator(device="cuda:0")
+    gen.manual_seed(4)
+    proj = torch.empty((B * S, n), dtype=torch.bfloat16, device="cuda").normal_(0.0, 1.0, generator=gen)
+    conv = torch.empty((2 * nh * dh + nv * dh, c["conv"]), dtype=torch.bfloat16, device="cuda").normal_(0.0, 0.5,
+                                                                                                     generator=gen)
+    a_log = torch.empty(nv, device="cuda").uniform_(0.01, 0.3, generator=gen).log().to(torch.bfloat16)
+    dt_bias = torch.zeros(nv, dtype=torch.bfloat16, device="cuda")
+    norm_w = torch.ones(dh, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty((B * S, nv * dh), dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def run():
+        _lib.check(lib.clef_op_gdn_core(_lib.DTYPE_BF16, proj.data_ptr(), n, conv.data_ptr(), c["conv"], a_log.data_ptr(),
+                                        dt_bias.data_ptr(), norm_w.data_ptr(), out.data_ptr(), B, S, nh, nv, dh,
+                                        ctypes.c_float(1e-6), stream.cuda_stream))
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            run()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    flops = gdn_flops(c)
+    clk = clocks.summary()
+    # FP32 CUDA-core peak at the sampled clock: 148 SMs x 128 FP32 lanes x 2 FLOP per FMA
+    fp32_peak = 148 * 128 * 2 * clk["sm_mhz"] * 1e6 / 1e12 if clk.get("sm_mhz") else None
+    moved = proj.numel() * 2 + out.numel() * 2
+    print(json.dumps({"metric": "Gated DeltaNet core throughput (B8 S2048, 16 key / 32 value heads x128)",
+                      "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps,
+                      "warmup": args.warmup, "dtype": "bf16 I/O, fp32 recurrence", "data": "synthetic",
+                      "flops_per_launch": flops, "frac_of_fp32_cuda_core_peak_at_sampled_clock":
+                      (flops / (ms / 1e3) / 1e12 / fp32_peak) if fp32_peak else None,
+                      "hbm_bytes_per_launch": moved, "achieved_gbs": moved / (ms / 1e3) / 1e9, "clocks": clk,
+                      "gpu_launches": args.steps}), flush=True)
+
+
 def traffic_per_launch():
     """DRAM bytes per gate/up launch from the committed ncu summary, if present."""
     p = ROOT / "profiles" / "gemm_gate_up_m16384.md"
@@ -540,9 +613,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("cfg2", "cfg3", "attention"), default="cfg2",
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "attention", "gdn"), default="cfg2",
                     help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark; "
-                    "attention = cfg2's attention layer alone")
+                    "attention = cfg2's attention layer alone; gdn = one Gated DeltaNet core")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -550,6 +623,8 @@ def main() -> None:
         gemm_arm(args)
     elif args.workload == "attention":
         attention_arm(args)
+    elif args.workload == "gdn":
+        gdn_arm(args)
     else:
         gpu_arm(args)
 

@@ -2042,6 +2042,9 @@ int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int
     REQUIRE(nh > 0 && nv > 0 && dh > 0 && nv % nh == 0, "Gated DeltaNet value heads must divide into key head groups");
     const long long need = 2LL * nh * dh + 2LL * nv * dh + 2LL * nv;
     REQUIRE(ldp >= need, "ldp is smaller than the packed projection width");
+    const int vec = dtype == CLEF_DTYPE_BF16 ? 8 : 4;
+    REQUIRE(ldp % vec == 0 && (reinterpret_cast<uintptr_t>(proj) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0,
+            "Gated DeltaNet rows must be 16-byte aligned (ldp a multiple of 16 bytes)");
     clef::Launcher L{static_cast<cudaStream_t>(stream), nullptr, 0};
     clef::GdnArgs a{};
     a.proj = proj;

@@ -235,7 +235,8 @@ int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out
  * that column order) to the gated, normalised output out [b*s, nv*dh] that
  * feeds out_proj.  conv [2*nh*dh + nv*dh, width] holds the q, k and v conv
  * rows; A_log, dt_bias [nv]; norm_w [dh].  dh = key = value head dim, one of
- * 8, 16, 32, 64, 128; nv % nh == 0; width 1..8. */
+ * 8, 16, 32, 64, 128; nv % nh == 0; width 1..8; proj and out 16-byte aligned
+ * and ldp * element size a multiple of 16 bytes. */
 int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int width, const void* A_log,
                      const void* dt_bias, const void* norm_w, void* out, int b, int s, int nh, int nv, int dh, float eps,
                      void* stream);

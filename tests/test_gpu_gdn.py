@@ -75,10 +75,13 @@ def test_gdn_core_matches_oracle(case, dtype):
     lib = _lib.load()
     import torch
 
-    tp, tc, ta, tb, tw = (dev(x, dtype) for x in (proj.reshape(b * s, -1), conv, A_log, dt_bias, norm_w))
+    ldp = -(-proj.shape[-1] // 16) * 16  # 16-byte rows in either dtype
+    padded = np.zeros((b * s, ldp), np.float32)
+    padded[:, : proj.shape[-1]] = proj.reshape(b * s, -1)
+    tp, tc, ta, tb, tw = (dev(x, dtype) for x in (padded, conv, A_log, dt_bias, norm_w))
     out = torch.full((b * s, nv * dh), float("nan"), device="cuda", dtype=tp.dtype)
     dt = _lib.DTYPE_BF16 if dtype == "bf16" else _lib.DTYPE_F32
-    _lib.check(lib.clef_op_gdn_core(dt, tp.data_ptr(), proj.shape[-1], tc.data_ptr(), width, ta.data_ptr(), tb.data_ptr(),
+    _lib.check(lib.clef_op_gdn_core(dt, tp.data_ptr(), ldp, tc.data_ptr(), width, ta.data_ptr(), tb.data_ptr(),
                                     tw.data_ptr(), out.data_ptr(), b, s, nh, nv, dh, ctypes.c_float(1e-6), None))
     got = host(out).reshape(expected.shape)
     scale = float(np.abs(expected).max())
