@@ -139,7 +139,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 
-def build_model(device: int):
+def build_model(device: int, max_seq_len: int = SEQ):
     """cfg2 in BF16: backbone weights drawn on the GPU (torch RNG), head from NumPy."""
     import torch
 
@@ -151,7 +151,7 @@ def build_model(device: int):
     build_lib()
     config = TextConfig.full_attention(**CFG2)
     head = HeadConfig(**HEAD)
-    model = ClefCudaModel(config, head, dtype="bf16", device=device, max_seq_len=SEQ)
+    model = ClefCudaModel(config, head, dtype="bf16", device=device, max_seq_len=max_seq_len)
     gen = torch.Generator(device=f"cuda:{device}")
     gen.manual_seed(WEIGHT_SEED)
     D, F, hq, hkv, d, V = (CFG2[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads", "head_dim", "vocab_size"))
@@ -523,6 +523,157 @@ def attention_arm(args) -> None:
                       "dtype": "bf16", "data": "synthetic", "gpu_launches": args.steps}), flush=True)
 
 
+CFG5 = {"states": 256, "median": 600, "sigma": 0.8, "min": 32, "max": 16384, "seed": 5, "long": 4}
+
+
+def serving_records(lengths, vocab: int, seed: int):
+    """Encoded records of the given lengths (uniform token ids) whose last 32
+    tokens hold 4 choice fields: 4 tokens of question span, then 4
+    single-token options each (the cfg2 layout), and the matching schema."""
+    from deciax_b200.clef_input import Field, Record
+
+    rng = np.random.default_rng(seed)
+    questions = {f"q{k}": {"type": "choice", "criteria": {c: f"option {c}" for c in "abcd"}} for k in range(QUESTIONS)}
+    records = []
+    for n in lengths:
+        ids = rng.integers(0, vocab, size=int(n), dtype=np.int64)
+        fields = []
+        for k in range(QUESTIONS):
+            off = int(n) - 8 * QUESTIONS + 8 * k
+            fields.append(Field(f"q{k}", 1, (off, off + 4), tuple((off + 4 + j, off + 5 + j) for j in range(OPTIONS)),
+                                tuple("abcd")))
+        records.append(Record(tuple(int(i) for i in ids), tuple(fields)))
+    return records, questions
+
+
+def serving_arm(args) -> None:
+    """BASELINE cfg5: decide_batch of 256 states with lognormal lengths (median
+    600, sigma 0.8, clipped to [32, 16384], seed 5), 4 choice x 4 options
+    each, through ClefEngine (length-grouped batches, host arrays in, answers
+    out), plus the max_len case of 4 x 16384 tokens.  Under torchrun each rank
+    (one GPU, a full replica) serves every N-th state: data parallel, max over
+    ranks.  Reports decisions/s and p50/p99 per-batch latency."""
+    import torch
+
+    from deciax_b200.engine import ClefEngine
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
+    c = CFG5
+    rng = np.random.default_rng(c["seed"])
+    lengths = np.clip(np.round(rng.lognormal(np.log(c["median"]), c["sigma"], c["states"])), c["min"], c["max"]).astype(int)
+    sweep, questions = serving_records(lengths[rank::world], CFG2["vocab_size"], seed=10 + rank)
+    longs, _ = serving_records([c["max"]] * c["long"], CFG2["vocab_size"], seed=20)
+    longs = longs[rank::world]
+    model = build_model(local, max_seq_len=c["max"])
+    engine = ClefEngine(model)
+
+    def run(records, timings=None):
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        answers = engine.decide_records(records, questions, timings) if records else []
+        elapsed = time.perf_counter() - t0
+        return answers, elapsed
+
+    for _ in range(args.warmup):
+        run(sweep)
+        run(longs)
+    sweep_t, long_t, timings, long_timings = [], [], [], []
+    for _ in range(args.steps):
+        answers, t = run(sweep, timings)
+        sweep_t.append(t)
+        _, t = run(longs, long_timings)
+        long_t.append(t)
+    assert all(len(a["answers"]) == QUESTIONS for a in answers)
+
+    def agg(v: float, op: str) -> float:
+        if not dist:
+            return v
+        x = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(x, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+        return float(x.item())
+
+    def pct(vals, q):
+        return float(np.percentile(np.asarray(vals) * 1e3, q)) if vals else 0.0
+
+    sweep_s = agg(statistics.mean(sweep_t), "max")
+    long_s = agg(statistics.mean(long_t), "max")
+    decisions = agg(float(len(sweep) * QUESTIONS), "sum")
+    tokens = agg(float(sum(len(r.ids) for r in sweep)), "sum")
+    p50, p99 = agg(pct([t for *_, t in timings], 50), "max"), agg(pct([t for *_, t in timings], 99), "max")
+    lp50 = agg(pct([t for *_, t in long_timings], 50), "max")
+    if dist:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "cfg5 serving sweep: decisions/s (decide_batch of 256 lognormal-length states)",
+            "value": decisions / sweep_s, "unit": "decisions/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic (random-init weights, uniform token ids, lognormal lengths)",
+            "config": {"workload": "cfg5", "states": c["states"], "lengths": "lognormal(log 600, 0.8) clipped [32, 16384], seed 5",
+                       "total_tokens": int(lengths.sum()), "parallelism": f"dp{world}" if world > 1 else "single",
+                       "batching": "ClefEngine length-grouped, max_batch_tokens 65536"},
+            "prefill_tokens_per_s": tokens / sweep_s, "sweep_seconds": sweep_s,
+            "batch_latency_ms": {"p50": p50, "p99": p99, "batches_per_rank": len(timings) // max(args.steps, 1)},
+            "max_len_case": {"states": c["long"], "tokens_per_state": c["max"], "seconds": long_s,
+                             "decisions_per_s": c["long"] * QUESTIONS / long_s, "batch_latency_ms_p50": lp50},
+            "timing": "host wall clock around ClefEngine.decide_records (collate, H2D, forward, D2H, decode)",
+        }), flush=True)
+
+
+def rmsnorm_arm(args) -> None:
+    """cfg2's RMSNorm alone (the memory-bound kernel run 85 times per step):
+    [16384, 3584] bf16 in and out (235 MB, larger than L2), through
+    clef_op_rmsnorm; achieved GB/s = (read + write bytes) / time."""
+    import torch
+
+    from deciax_b200 import _lib
+    from deciax_b200.build import build as build_lib
+
+    build_lib()
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    rows, dim = STATES * SEQ, CFG2["hidden_size"]
+    gen = torch.Generator(device="cuda:0")
+    gen.manual_seed(6)
+    x = torch.empty((rows, dim), dtype=torch.bfloat16, device="cuda").normal_(0.0, 1.0, generator=gen)
+    w = torch.empty(dim, dtype=torch.bfloat16, device="cuda").normal_(0.0, 0.02, generator=gen)
+    out = torch.empty_like(x)
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def run():
+        _lib.check(lib.clef_op_rmsnorm(_lib.DTYPE_BF16, x.data_ptr(), w.data_ptr(), out.data_ptr(), rows, dim,
+                                       ctypes.c_float(1e-6), stream.cuda_stream))
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        run()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    moved = 2 * rows * dim * 2 + dim * 2
+    peaks = measured_peaks()
+    print(json.dumps({"metric": "cfg2 RMSNorm bandwidth ([16384, 3584] bf16)", "value": moved / (ms / 1e3) / 1e9,
+                      "unit": "GB/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "frac_of_measured_hbm": moved / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "bytes_per_launch": moved,
+                      "dtype": "bf16", "data": "synthetic", "gpu_launches": args.steps}), flush=True)
+
+
 GDN = {"states": 8, "seq": 2048, "key_heads": 16, "value_heads": 32, "head_dim": 128, "conv": 4}
 
 
@@ -613,9 +764,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("cfg2", "cfg3", "attention", "gdn"), default="cfg2",
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg5", "attention", "gdn", "rmsnorm"), default="cfg2",
                     help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark; "
-                    "attention = cfg2's attention layer alone; gdn = one Gated DeltaNet core")
+                    "cfg5 = the serving sweep through ClefEngine; attention = cfg2's attention layer alone; "
+                    "gdn = one Gated DeltaNet core; rmsnorm = cfg2's RMSNorm alone")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -625,6 +777,10 @@ def main() -> None:
         attention_arm(args)
     elif args.workload == "gdn":
         gdn_arm(args)
+    elif args.workload == "cfg5":
+        serving_arm(args)
+    elif args.workload == "rmsnorm":
+        rmsnorm_arm(args)
     else:
         gpu_arm(args)
 

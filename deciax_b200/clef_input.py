@@ -195,12 +195,17 @@ def encode(tokenizer: Any, state: Any, questions: Mapping[str, Any], max_length:
     return prompt.record(prompt.tokens(render(state)), max_length)
 
 
-def collate(records: Sequence[Record], pad_id: int) -> dict[str, np.ndarray]:
+def collate(records: Sequence[Record], pad_id: int, *, rows: int | None = None, seq_len: int | None = None) -> dict[str, np.ndarray]:
     """Pad records to bucketed shapes; options are flat with explicit field
     ownership and lexical spans index a compact per-row token list
-    (input.py:139-182)."""
-    b = bucket(len(records), ROW_BUCKETS)
-    s = bucket(max(len(r.ids) for r in records), SEQUENCE_BUCKETS)
+    (input.py:139-182).  ``rows`` / ``seq_len`` override the row and sequence
+    buckets (the CUDA model takes any shape; padding never changes a row's
+    logits), e.g. to pad only to a multiple of 128 tokens."""
+    longest = max(len(r.ids) for r in records)
+    b = bucket(len(records), ROW_BUCKETS) if rows is None else rows
+    s = bucket(longest, SEQUENCE_BUCKETS) if seq_len is None else seq_len
+    if b < len(records) or s < longest:
+        raise ValueError("rows / seq_len smaller than the records")
     q = bucket(max(len(r.fields) for r in records), SCHEMA_BUCKETS)
     o = bucket(max(sum(len(f.option_ids) for f in r.fields) for r in records), SCHEMA_BUCKETS)
     option_spans = [[span for f in r.fields for span in f.option_spans] for r in records]

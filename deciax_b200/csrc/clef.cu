@@ -368,6 +368,20 @@ static void gemm_simt(Launcher& L, int epi, const T* A, int lda, const T* B, int
 template <typename T>
 static void rmsnorm(Launcher& L, const T* x, int ldx, const T* w, T* out, int ldo, int rows, int dim, float eps,
                     const uint8_t* row_mask = nullptr) {
+  if constexpr (sizeof(T) == 2) {
+    if (dim % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && dim <= kRmsSmemMaxDim && aligned16(x) && aligned16(w) &&
+        aligned16(out)) {
+      const size_t smem = static_cast<size_t>(kRmsSmemRows) * dim * 2;  // one staged row per warp
+      if (smem > 48 * 1024)
+        CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bf16_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+      rmsnorm_bf16_smem_kernel<<<(rows + kRmsSmemRows - 1) / kRmsSmemRows, 32 * kRmsSmemRows, smem, L.stream>>>(
+          x, ldx, w, out, ldo, rows, dim, eps, row_mask);
+      CUDA_CHECK(cudaGetLastError());
+      L.tick();
+      return;
+    }
+  }
   const int warps = 8;
   rmsnorm_kernel<T><<<(rows + warps - 1) / warps, warps * 32, 0, L.stream>>>(x, ldx, w, out, ldo, rows, dim, eps,
                                                                             row_mask);

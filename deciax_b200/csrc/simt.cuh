@@ -146,6 +146,58 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, int ldx, const T* __rest
   for (int i = lane; i < dim; i += 32) orow[i] = from_f32<T>(to_f32(xr[i]) * r * (to_f32(w[i]) + 1.f));
 }
 
+// The same RMSNorm for bf16 rows of at most kRmsSmemMaxDim elements (dim and
+// ldx multiples of 8): each warp stages its row in shared memory with 16-byte
+// cp.async copies all in flight, then reads it twice from there, so DRAM sees
+// one read of x.  4 rows (warps) per block.
+constexpr int kRmsSmemMaxDim = 8192;
+constexpr int kRmsSmemRows = 4;
+__global__ void __launch_bounds__(32 * kRmsSmemRows)
+    rmsnorm_bf16_smem_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
+                             __nv_bfloat16* __restrict__ out, int ldo, int rows, int dim, float eps,
+                             const uint8_t* __restrict__ row_mask) {
+  extern __shared__ uint4 rms_stage[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRmsSmemRows + warp;
+  if (row >= rows) return;
+  const int nvec = dim / 8;
+  uint4* buf = rms_stage + static_cast<size_t>(warp) * nvec;
+  __nv_bfloat16* orow = out + static_cast<size_t>(row) * ldo;
+  if (row_mask != nullptr && row_mask[row] == 0) {
+    for (int v = lane; v < nvec; v += 32) reinterpret_cast<uint4*>(orow)[v] = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx);
+  for (int v = lane; v < nvec; v += 32) cp_async16(buf + v, xr + v, true);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
+  float ss = 0.f;
+  for (int v = lane; v < nvec; v += 32) {
+    const uint4 q = buf[v];
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = __bfloat162float(h[j]);
+      ss += f * f;
+    }
+  }
+  const float r = rsqrtf(warp_sum(ss) / dim + eps);
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  for (int v = lane; v < nvec; v += 32) {
+    const uint4 q = buf[v];
+    const uint4 wq = wv[v];
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&q);
+    const __nv_bfloat16* wh = reinterpret_cast<const __nv_bfloat16*>(&wq);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = pack_bf16x2(__bfloat162float(h[2 * j]) * r * (__bfloat162float(wh[2 * j]) + 1.f),
+                         __bfloat162float(h[2 * j + 1]) * r * (__bfloat162float(wh[2 * j + 1]) + 1.f));
+    reinterpret_cast<uint4*>(orow)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // LayerNorm with weight and bias, eps 1e-5 (nn.py:22-28, head.py:16-17).
 template <typename T>
 __global__ void layernorm_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,

@@ -9,8 +9,9 @@ other rows or the padding of its batch:
 * the schema is tokenised once per call and the states as one tokenizer batch
   (``SchemaPrompt.encode_states``) instead of one full ``encode`` per state;
 * records are grouped by length into batches whose padded size
-  (rows x sequence bucket) stays within ``max_batch_tokens``, with row counts
-  that fill a row bucket exactly, instead of fixed pairs in input order;
+  (rows x padded length) stays within ``max_batch_tokens``, instead of fixed
+  pairs in input order; a batch is padded only to its longest record rounded
+  up to 128 tokens (not to a power-of-two bucket) and has no padded rows;
 * batches go to every replica at once (data parallelism: one model per GPU,
   each with full weights, no collective), one host thread per replica.  The
   library releases the GIL for the whole forward, so replicas run
@@ -27,36 +28,40 @@ from __future__ import annotations
 
 import queue
 import threading
+import time
 from collections.abc import Mapping, Sequence
 from concurrent.futures import ThreadPoolExecutor
 from typing import Any
 
 import numpy as np
 
-from deciax_b200.clef_input import ROW_BUCKETS, SEQUENCE_BUCKETS, Record, SchemaPrompt, bucket, collate, decode
+from deciax_b200.clef_input import ROW_BUCKETS, Record, SchemaPrompt, collate, decode
 
 DEFAULT_BATCH_TOKENS = 65536
+SEQ_ALIGN = 128
 
 
-def plan_batches(lengths: Sequence[int], max_batch_tokens: int = DEFAULT_BATCH_TOKENS,
-                 max_rows: int = ROW_BUCKETS[-1]) -> list[list[int]]:
-    """Group record indices into batches, longest first.
+def plan_batches(lengths: Sequence[int], max_batch_tokens: int = DEFAULT_BATCH_TOKENS, max_rows: int = ROW_BUCKETS[-1],
+                 seq_align: int = SEQ_ALIGN, fill: float = 0.75) -> list[tuple[list[int], int]]:
+    """Group record indices into (indices, padded length) batches, longest first.
 
-    Each batch holds records of similar length; its row count is a row bucket
-    (no padded rows) unless fewer records remain, and rows x the sequence
-    bucket of its longest record stays within ``max_batch_tokens`` (a single
-    record longer than the budget gets a batch of its own).
+    A batch's padded length is its longest record rounded up to ``seq_align``;
+    later (shorter) records join while the batch stays within
+    ``max_batch_tokens`` and ``max_rows`` and each is at least ``fill`` of the
+    longest, so padding stays bounded.  A record longer than the budget
+    runs alone.
     """
     order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
-    batches: list[list[int]] = []
+    batches: list[tuple[list[int], int]] = []
     pos = 0
     while pos < len(order):
-        seq = bucket(lengths[order[pos]], SEQUENCE_BUCKETS)
+        seq = -(-lengths[order[pos]] // seq_align) * seq_align
         cap = max(1, min(max_rows, max_batch_tokens // seq))
-        limit = min(cap, len(order) - pos)
-        rows = max(r for r in ROW_BUCKETS if r <= limit)
-        batches.append(order[pos : pos + rows])
-        pos += rows
+        end = pos + 1
+        while end < len(order) and end - pos < cap and lengths[order[end]] >= fill * lengths[order[pos]]:
+            end += 1
+        batches.append((order[pos:end], seq))
+        pos = end
     return batches
 
 
@@ -79,19 +84,26 @@ class ClefEngine:
                      head_max_len: int | None = None) -> list[dict[str, Any]]:
         if head_max_len is not None:
             raise ValueError("Clef has one joint token budget; head_max_len is unsupported")
-        records = self.encode(states, questions, max_len)
+        return self.decide_records(self.encode(states, questions, max_len), questions)
+
+    def decide_records(self, records: Sequence[Record], questions: Mapping[Any, Mapping[str, Any]],
+                       timings: list | None = None) -> list[dict[str, Any]]:
+        """Answers for already-encoded records, in input order.  With
+        ``timings``, each batch appends (rows, sequence bucket, seconds of its
+        forward, host arrays in and logits out)."""
         if not records:
             return []
         batches = plan_batches([len(r.ids) for r in records], self.max_batch_tokens)
         results: list[dict[str, Any] | None] = [None] * len(records)
-        work: queue.Queue[list[int]] = queue.Queue()
+        work: queue.Queue[tuple[list[int], int]] = queue.Queue()
         for b in batches:
             work.put(b)
         errors: list[BaseException] = []
         pad_id, name = self.model.pad_token_id, self.model.name
 
-        def prepare(idx: list[int]) -> tuple[list[int], dict[str, np.ndarray]]:
-            return idx, collate([records[i] for i in idx], pad_id)
+        def prepare(batch: tuple[list[int], int]) -> tuple[list[int], dict[str, np.ndarray]]:
+            idx, seq = batch
+            return idx, collate([records[i] for i in idx], pad_id, rows=len(idx), seq_len=seq)
 
         def serve(k: int) -> None:
             replica, lock = self.replicas[k], self._locks[k]
@@ -109,7 +121,10 @@ class ClefEngine:
                     except queue.Empty:
                         pending = None
                     with lock:
+                        t0 = time.perf_counter()
                         logits = np.asarray(replica.forward(arrays), np.float32)
+                        if timings is not None:
+                            timings.append((len(idx), arrays["input_ids"].shape[1], time.perf_counter() - t0))
                     for row, i in enumerate(idx):
                         results[i] = decode(records[i], logits[row], questions, name)
 

@@ -193,15 +193,15 @@ def states(n, seed=0):
     return [" ".join(rng.choice(words, size=int(rng.integers(1, 400)))) for _ in range(n)]
 
 
-def test_plan_batches_fills_row_buckets_within_budget():
+def test_plan_batches_bounds_padding_and_budget():
     lengths = [int(x) for x in np.random.default_rng(3).integers(50, 9000, size=137)]
     batches = plan_batches(lengths, max_batch_tokens=32768)
-    assert sorted(i for b in batches for i in b) == list(range(137))
-    for b in batches:
-        seq = I.bucket(max(lengths[i] for i in b), I.SEQUENCE_BUCKETS)
-        assert len(b) in I.ROW_BUCKETS
-        assert len(b) * seq <= 32768 or len(b) == 1
-    assert plan_batches([20000 - 3616], 1024) == [[0]]  # one over-budget record runs alone
+    assert sorted(i for idx, _ in batches for i in idx) == list(range(137))
+    for idx, seq in batches:
+        assert seq % 128 == 0 and max(lengths[i] for i in idx) <= seq < max(lengths[i] for i in idx) + 128
+        assert len(idx) * seq <= 32768 or len(idx) == 1
+        assert all(lengths[i] >= 0.75 * lengths[idx[0]] for i in idx[1:])
+    assert plan_batches([16384], 1024) == [([0], 16384)]  # one over-budget record runs alone
 
 
 def test_engine_matches_per_record_answers_in_input_order():
@@ -210,7 +210,7 @@ def test_engine_matches_per_record_answers_in_input_order():
     ss = states(23) + FIX["states"]
     got = ClefEngine(model, max_batch_tokens=4096).decide_batch(ss, questions)
     assert got == expected_answers(FakeReplica(TOK), ss, questions)
-    assert all(b in I.ROW_BUCKETS for b, _ in model.calls)
+    assert all(s % 128 == 0 for _, s in model.calls)
     assert len(model.calls) < len(ss) // 2  # larger batches than the reference's fixed pairs
 
 
