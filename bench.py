@@ -139,8 +139,11 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 
-def build_model(device: int, max_seq_len: int = SEQ):
-    """cfg2 in BF16: backbone weights drawn on the GPU (torch RNG), head from NumPy."""
+def build_model(device: int, max_seq_len: int = SEQ, cfg: dict | None = None, tp_rank: int = 0, tp_size: int = 1,
+                nccl_id: bytes | None = None):
+    """cfg2 (or ``cfg``) in BF16: backbone weights drawn on the GPU (torch RNG,
+    the same full tensors on every tensor-parallel rank, which keeps its
+    shard), head from NumPy."""
     import torch
 
     from deciax_b200.build import build as build_lib
@@ -149,12 +152,14 @@ def build_model(device: int, max_seq_len: int = SEQ):
     from deciax_b200.synthetic import synthetic_head_weights
 
     build_lib()
-    config = TextConfig.full_attention(**CFG2)
+    cfg = cfg or CFG2
+    config = TextConfig.full_attention(**cfg)
     head = HeadConfig(**HEAD)
-    model = ClefCudaModel(config, head, dtype="bf16", device=device, max_seq_len=max_seq_len)
+    model = ClefCudaModel(config, head, dtype="bf16", device=device, max_seq_len=max_seq_len, tp_rank=tp_rank,
+                          tp_size=tp_size, nccl_id=nccl_id)
     gen = torch.Generator(device=f"cuda:{device}")
     gen.manual_seed(WEIGHT_SEED)
-    D, F, hq, hkv, d, V = (CFG2[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads", "head_dim", "vocab_size"))
+    D, F, hq, hkv, d, V = (cfg[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads", "head_dim", "vocab_size"))
 
     def randn(*shape):
         t = torch.empty(shape, dtype=torch.bfloat16, device=f"cuda:{device}")
@@ -171,7 +176,7 @@ def build_model(device: int, max_seq_len: int = SEQ):
         "mixer.q_norm.weight": (d,), "mixer.k_norm.weight": (d,), "mlp.gate_proj.weight": (F, D),
         "mlp.up_proj.weight": (F, D), "mlp.down_proj.weight": (D, F),
     }
-    for i in range(CFG2["num_layers"]):
+    for i in range(cfg["num_layers"]):
         for name, shape in shapes.items():
             model.upload_device(f"layers.{i}.{name}", randn(*shape))
     for k, v in synthetic_head_weights(D, head, seed=WEIGHT_SEED, std=WEIGHT_STD, dtype="bf16").items():
@@ -674,6 +679,128 @@ def rmsnorm_arm(args) -> None:
                       "dtype": "bf16", "data": "synthetic", "gpu_launches": args.steps}), flush=True)
 
 
+CFG4 = dict(hidden_size=4608, intermediate_size=36864, num_attention_heads=32, num_key_value_heads=16, head_dim=128,
+            num_layers=46, vocab_size=256000)
+CFG4_BATCH = {"states": 16, "seq": 8192, "choice": (8, 24), "score": (24, 8), "noul": 32}
+
+
+def mixed_records(states: int, length: int, vocab: int, seed: int):
+    """cfg4 records: per state `length` uniform token ids ending in 64 fields
+    (8 choice x 24 options, 24 score x 8 levels, 32 noul x 2 = 448 options);
+    each field is 4 tokens of question span followed by one token per option."""
+    from deciax_b200.clef_input import Field, Record
+
+    rng = np.random.default_rng(seed)
+    c = CFG4_BATCH
+    kinds = [(1, c["choice"][1])] * c["choice"][0] + [(2, c["score"][1])] * c["score"][0] + [(0, 2)] * c["noul"]
+    schema = sum(4 + n for _, n in kinds)
+    records = []
+    for _ in range(states):
+        ids = rng.integers(0, vocab, size=length, dtype=np.int64)
+        off, fields = length - schema, []
+        for k, (kind, n) in enumerate(kinds):
+            oids = ("true", "false") if kind == 0 else tuple(str(j) for j in range(n))
+            fields.append(Field(f"f{k}", kind, (off, off + 4), tuple((off + 4 + j, off + 5 + j) for j in range(n)), oids))
+            off += 4 + n
+        records.append(Record(tuple(int(i) for i in ids), tuple(fields)))
+    return records
+
+
+def cfg4_arm(args) -> None:
+    """BASELINE cfg4: the clef-shaped 27B model (46 layers, hidden 4608, 32 q /
+    16 kv heads of 128, MLP 36864, vocab 256000), BF16, tensor-parallel over
+    the N ranks of torchrun (heads and MLP columns sharded, FP32 all-reduce of
+    the o-proj and down-proj partials over NCCL), one batch of 16 states x
+    8192 tokens per step (64 fields, 448 options per state).  Strong scaling:
+    the work per step is fixed; value = the group's tokens/s."""
+    import ctypes as ct
+
+    import torch
+
+    from deciax_b200 import _lib
+    from deciax_b200.clef_input import collate
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    nccl_id = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
+        obj = [None]
+        if rank == 0:
+            buf = ct.create_string_buffer(_lib.NCCL_ID_BYTES)
+            _lib.check(_lib.load().clef_nccl_unique_id(buf))
+            obj = [buf.raw]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    c = CFG4_BATCH
+    model = build_model(local, max_seq_len=c["seq"], cfg=CFG4, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
+    arrays = collate(mixed_records(c["states"], c["seq"], CFG4["vocab_size"], seed=31), 0)
+    tensors = {k: torch.from_numpy(np.ascontiguousarray(arrays[k]).astype(np.uint8 if arrays[k].dtype == bool else np.int32)).cuda()
+               for k in _lib.BATCH_KEYS}
+    out = torch.empty(arrays["option_mask"].shape, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        model.forward_device(tensors, out, stream.cuda_stream)
+    torch.cuda.synchronize()
+    model.check_status()
+    barrier()
+    model.set_timing(True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            model.forward_device(tensors, out, stream.cuda_stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    timing = model.timing_report()
+    model.set_timing(False)
+    model.check_status()
+    logits = out.cpu().numpy()
+    if not np.isfinite(logits[arrays["option_mask"]]).all():
+        raise SystemExit("non-finite logits")
+    if dist:
+        x = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        ms = float(x.item())
+    tokens = c["states"] * c["seq"]
+    linear, attention, _ = algorithmic_flops(CFG4, [c["seq"]] * c["states"])
+    flops = linear + attention
+    peaks = measured_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "cfg4 27B-shaped prefill+scoring tokens/s (tensor parallel)", "value": tokens / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic (random-init weights, uniform token ids)",
+            "config": {"workload": "cfg4: 46 layers, D4608, 32q/16kv x128, F36864, V256000; 16 x 8192 tokens; 64 fields / 448 "
+                       "options per state (8 choice x 24, 24 score x 8, 32 noul)", "parallelism": f"tp{world}"},
+            "decisions_per_s": c["states"] * 64 / (ms / 1e3),
+            "tensor_frac": {"flops_per_step": flops, "achieved_tflops": flops / (ms / 1e3) / 1e12,
+                            "frac_of_measured_burst_x_gpus": flops / (ms / 1e3) / 1e12 / (peaks["bf16_tflops"] * world)},
+            "kernel_ms_per_step_rank0": {k: round(v[0] / args.steps, 3) for k, v in timing.items() if v[1]},
+            "clocks": clocks.summary(), "gpu_launches": model.last_launch_count * args.steps,
+        }), flush=True)
+    if dist:
+        model.close()
+        dist.destroy_process_group()
+
+
 GDN = {"states": 8, "seq": 2048, "key_heads": 16, "value_heads": 32, "head_dim": 128, "conv": 4}
 
 
@@ -764,10 +891,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg5", "attention", "gdn", "rmsnorm"), default="cfg2",
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg4", "cfg5", "attention", "gdn", "rmsnorm"), default="cfg2",
                     help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark; "
                     "cfg5 = the serving sweep through ClefEngine; attention = cfg2's attention layer alone; "
-                    "gdn = one Gated DeltaNet core; rmsnorm = cfg2's RMSNorm alone")
+                    "gdn = one Gated DeltaNet core; rmsnorm = cfg2's RMSNorm alone; cfg4 = the 27B-shaped model, "
+                    "tensor parallel over the torchrun ranks")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -781,6 +909,8 @@ def main() -> None:
         serving_arm(args)
     elif args.workload == "rmsnorm":
         rmsnorm_arm(args)
+    elif args.workload == "cfg4":
+        cfg4_arm(args)
     else:
         gpu_arm(args)
 

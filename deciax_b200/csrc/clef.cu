@@ -37,6 +37,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm2_sm100.cuh"
 #include "gdn.cuh"
+#include "tp.cuh"
 #include "head.cuh"
 #include "simt.cuh"
 
@@ -674,7 +675,62 @@ struct Model {
     timeline.cats.clear();
   }
 
+  // Peer pointers of the TP workspace (CUDA IPC): every rank's FP32 partial
+  // and residual stream, refreshed whenever the local buffers move.
+  void* ipc_part_src = nullptr;
+  void* ipc_x_src = nullptr;
+  std::vector<void*> peer_part, peer_x;
+  DBuf ipc_scratch, barrier_buf;
+  bool p2p = false;  // peer pointers valid: TP reduction through tp_reduce_residual_kernel
+
+  void close_peers() {
+    for (int k = 0; k < static_cast<int>(peer_part.size()); ++k) {
+      if (k == rank) continue;
+      if (peer_part[k]) cudaIpcCloseMemHandle(peer_part[k]);
+      if (peer_x[k]) cudaIpcCloseMemHandle(peer_x[k]);
+    }
+    peer_part.assign(tp, nullptr);
+    peer_x.assign(tp, nullptr);
+    p2p = false;
+  }
+
+  // Collective over the TP group: all ranks call it with the same buffer sizes.
+  void exchange_ipc() {
+    close_peers();
+    cudaIpcMemHandle_t h[2];
+    CUDA_CHECK(cudaIpcGetMemHandle(&h[0], ws.partial.p));
+    CUDA_CHECK(cudaIpcGetMemHandle(&h[1], ws.x.p));
+    const size_t hb = sizeof(h);
+    ipc_scratch.ensure(static_cast<size_t>(tp) * hb);
+    uint8_t* d = ipc_scratch.as<uint8_t>();
+    CUDA_CHECK(cudaMemcpyAsync(d + rank * hb, h, hb, cudaMemcpyHostToDevice, stream));
+    NCCL_CHECK(ncclAllGather(d + rank * hb, d, hb, ncclUint8, comm, stream));
+    std::vector<uint8_t> all(static_cast<size_t>(tp) * hb);
+    CUDA_CHECK(cudaMemcpyAsync(all.data(), d, all.size(), cudaMemcpyDeviceToHost, stream));
+    CUDA_CHECK(cudaStreamSynchronize(stream));
+    for (int k = 0; k < tp; ++k) {
+      if (k == rank) {
+        peer_part[k] = ws.partial.p;
+        peer_x[k] = ws.x.p;
+        continue;
+      }
+      cudaIpcMemHandle_t hk[2];
+      std::memcpy(hk, all.data() + k * hb, hb);
+      CUDA_CHECK(cudaIpcOpenMemHandle(&peer_part[k], hk[0], cudaIpcMemLazyEnablePeerAccess));
+      CUDA_CHECK(cudaIpcOpenMemHandle(&peer_x[k], hk[1], cudaIpcMemLazyEnablePeerAccess));
+    }
+    ipc_part_src = ws.partial.p;
+    ipc_x_src = ws.x.p;
+    p2p = true;
+  }
+
+  // Every rank of the TP group has reached this point of its stream.
+  void tp_barrier(Launcher& Lc) {
+    NCCL_CHECK(ncclAllReduce(barrier_buf.p, barrier_buf.p, 1, ncclFloat32, ncclSum, comm, Lc.stream));
+  }
+
   ~Model() {
+    if (tp > 1) close_peers();
     if (comm) ncclCommDestroy(comm);
     if (stream) cudaStreamDestroy(stream);
   }
@@ -762,6 +818,8 @@ struct Model {
       ncclUniqueId id;
       std::memcpy(&id, nccl_id, sizeof(id));
       NCCL_CHECK(ncclCommInitRank(&comm, tp, id, rank));
+      barrier_buf.alloc(256);
+      CUDA_CHECK(cudaMemset(barrier_buf.p, 0, 256));
     }
     embedding.alloc(static_cast<size_t>(V) * D * esz);
     lm_head.alloc(static_cast<size_t>(V) * D * esz);
@@ -1142,6 +1200,7 @@ struct Model {
     w.lx = std::max(w.lx, lx);
     w.o = std::max(w.o, o);
     w.q = std::max(w.q, q);
+    if (tp > 1 && tp <= kTpMaxRanks && (w.partial.p != ipc_part_src || w.x.p != ipc_x_src)) exchange_ipc();
   }
 
   // -------------------------------------------------------------------------
@@ -1456,6 +1515,34 @@ struct Model {
       gemm_bf16(Lc, kEpiF32, in, K, w, K, Tt, D, K, part, D, nullptr, nullptr, 0);
     else
       gemm_simt<T>(Lc, kSimtF32, in, K, w, K, Tt, D, K, part, D, nullptr, nullptr, 0);
+    if (p2p) {
+      // every rank's partial complete -> each rank reduces its rows from every
+      // rank's partial and writes them into every x -> every x complete
+      const int saved = Lc.cat;
+      tp_barrier(Lc);
+      Lc.mark(kCatAllReduce);  // barriers are timed as "allreduce", the reduction as "residual_add"
+      Lc.cat = kCatResidual;
+      TpReduceArgs a{};
+      for (int k = 0; k < tp; ++k) {
+        a.parts[k] = static_cast<const float*>(peer_part[k]);
+        a.xs[k] = peer_x[k];
+      }
+      a.tp = tp;
+      a.rank = rank;
+      const long long rows_per = (Tt + tp - 1) / tp;
+      const long long r0 = std::min<long long>(Tt, rows_per * rank), r1 = std::min<long long>(Tt, r0 + rows_per);
+      a.e0 = r0 * D;
+      a.e1 = r1 * D;
+      const long long vecs = (a.e1 - a.e0) / 4;
+      const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((vecs + 255) / 256, 148LL * 8)));
+      tp_reduce_residual_kernel<T><<<grid, 256, 0, Lc.stream>>>(a);
+      CUDA_CHECK(cudaGetLastError());
+      Lc.tick();
+      tp_barrier(Lc);
+      Lc.mark(kCatAllReduce);
+      Lc.cat = saved;
+      return;
+    }
     NCCL_CHECK(ncclAllReduce(part, part, static_cast<size_t>(Tt) * D, ncclFloat32, ncclSum, comm, Lc.stream));
     Lc.mark(kCatAllReduce);
     const long long n = static_cast<long long>(Tt) * D;

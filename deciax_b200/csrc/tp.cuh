@@ -1,0 +1,61 @@
+// Tensor-parallel reduction of the o-proj / down-proj partial products over
+// NVLink peer memory: the FP32 sum across ranks, the cast, and the residual
+// add of qwen3_5/pallas.py:66-69,121 (x = T(x + T(sum_k partial_k))), in one
+// kernel per rank instead of an NCCL all-reduce followed by an add kernel.
+//
+// Every rank owns a contiguous 1/tp share of the rows.  For each element of
+// its share it reads the tp FP32 partials (its own and, through CUDA IPC
+// pointers, each peer's) and sums them in rank order -- so the result is the
+// same bits on every rank -- adds its residual, casts, and stores the result
+// into every rank's residual stream x (its own copy and each peer's).  The
+// launch sits between two cross-rank barriers on the stream: before it every
+// rank's partial is complete, after it every rank's x is.  Plain 16/8-byte
+// peer loads and stores only; no multicast.  (Pushing the partials from the
+// GEMM epilogue into their owners' memory instead was measured slower: the
+// NVLink stores stall the epilogue.)
+#pragma once
+
+#include "common.cuh"
+
+namespace clef {
+
+constexpr int kTpMaxRanks = 8;
+
+struct TpReduceArgs {
+  const float* parts[kTpMaxRanks];  // rank k's FP32 partial [rows, dim]
+  void* xs[kTpMaxRanks];            // rank k's residual stream x [rows, dim]
+  int tp, rank;
+  long long e0, e1;  // this rank's element range, multiples of 4
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpReduceArgs a) {
+  const T* own = static_cast<const T*>(a.xs[a.rank]);
+  const long long stride = 4LL * gridDim.x * blockDim.x;
+  for (long long i = a.e0 + 4LL * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x); i < a.e1;
+       i += stride) {
+    float4 s = *reinterpret_cast<const float4*>(a.parts[0] + i);
+    for (int k = 1; k < a.tp; ++k) {
+      const float4 p = *reinterpret_cast<const float4*>(a.parts[k] + i);
+      s.x += p.x;
+      s.y += p.y;
+      s.z += p.z;
+      s.w += p.w;
+    }
+    if constexpr (sizeof(T) == 2) {
+      const uint2 rv = *reinterpret_cast<const uint2*>(own + i);
+      const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rv.x));
+      const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rv.y));
+      const uint2 o = make_uint2(pack_bf16x2(r0.x + round_to<T>(s.x), r0.y + round_to<T>(s.y)),
+                                 pack_bf16x2(r1.x + round_to<T>(s.z), r1.y + round_to<T>(s.w)));
+      for (int k = 0; k < a.tp; ++k) *reinterpret_cast<uint2*>(static_cast<T*>(a.xs[k]) + i) = o;
+    } else {
+      const float4 r = *reinterpret_cast<const float4*>(own + i);
+      const float4 o = make_float4(r.x + s.x, r.y + s.y, r.z + s.z, r.w + s.w);
+      for (int k = 0; k < a.tp; ++k) *reinterpret_cast<float4*>(static_cast<T*>(a.xs[k]) + i) = o;
+    }
+  }
+  __threadfence_system();  // peer stores ordered before the barrier that follows
+}
+
+}  // namespace clef
