@@ -34,25 +34,35 @@ __global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpReduceArgs a)
   const long long stride = 4LL * gridDim.x * blockDim.x;
   for (long long i = a.e0 + 4LL * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x); i < a.e1;
        i += stride) {
-    float4 s = *reinterpret_cast<const float4*>(a.parts[0] + i);
-    for (int k = 1; k < a.tp; ++k) {
-      const float4 p = *reinterpret_cast<const float4*>(a.parts[k] + i);
-      s.x += p.x;
-      s.y += p.y;
-      s.z += p.z;
-      s.w += p.w;
-    }
+    // every rank's partial in flight at once, then the sum in rank order
+    float4 p[kTpMaxRanks];
+#pragma unroll
+    for (int k = 0; k < kTpMaxRanks; ++k)
+      if (k < a.tp) p[k] = *reinterpret_cast<const float4*>(a.parts[k] + i);
+    float4 s = p[0];
+#pragma unroll
+    for (int k = 1; k < kTpMaxRanks; ++k)
+      if (k < a.tp) {
+        s.x += p[k].x;
+        s.y += p[k].y;
+        s.z += p[k].z;
+        s.w += p[k].w;
+      }
     if constexpr (sizeof(T) == 2) {
       const uint2 rv = *reinterpret_cast<const uint2*>(own + i);
       const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rv.x));
       const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rv.y));
       const uint2 o = make_uint2(pack_bf16x2(r0.x + round_to<T>(s.x), r0.y + round_to<T>(s.y)),
                                  pack_bf16x2(r1.x + round_to<T>(s.z), r1.y + round_to<T>(s.w)));
-      for (int k = 0; k < a.tp; ++k) *reinterpret_cast<uint2*>(static_cast<T*>(a.xs[k]) + i) = o;
+#pragma unroll
+      for (int k = 0; k < kTpMaxRanks; ++k)
+        if (k < a.tp) *reinterpret_cast<uint2*>(static_cast<T*>(a.xs[k]) + i) = o;
     } else {
       const float4 r = *reinterpret_cast<const float4*>(own + i);
       const float4 o = make_float4(r.x + s.x, r.y + s.y, r.z + s.z, r.w + s.w);
-      for (int k = 0; k < a.tp; ++k) *reinterpret_cast<float4*>(static_cast<T*>(a.xs[k]) + i) = o;
+#pragma unroll
+      for (int k = 0; k < kTpMaxRanks; ++k)
+        if (k < a.tp) *reinterpret_cast<float4*>(static_cast<T*>(a.xs[k]) + i) = o;
     }
   }
   __threadfence_system();  // peer stores ordered before the barrier that follows
