@@ -437,16 +437,22 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t off = (chunk >> 3) * (BQ * 128) + r * 128 + (((chunk & 7) ^ (r & 7)) << 4);
           uint32_t w[4];
           if (a.gate) {
+            // T(T(O / l) * T(sigmoid(gate))) on bf16 pairs: the product of two
+            // bf16 values is exact in FP32, so the packed multiply rounds once
+            // exactly as the scalar form
             const uint4 gq = *reinterpret_cast<const uint4*>(sK + off);
             const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
-              const float x0 = round_to<__nv_bfloat16>(__uint_as_float(o[v4 * 8 + 2 * e]) * inv);
-              const float x1 = round_to<__nv_bfloat16>(__uint_as_float(o[v4 * 8 + 2 * e + 1]) * inv);
-              const float s0 = a.gate_presig ? g.x : round_to<__nv_bfloat16>(sigmoid_fast(g.x));
-              const float s1 = a.gate_presig ? g.y : round_to<__nv_bfloat16>(sigmoid_fast(g.y));
-              w[e] = pack_bf16x2(x0 * s0, x1 * s1);
+              __nv_bfloat162 g2 = *reinterpret_cast<const __nv_bfloat162*>(&gw[e]);
+              if (!a.gate_presig) {
+                const float2 g = __bfloat1622float2(g2);
+                g2 = __floats2bfloat162_rn(sigmoid_fast(g.x), sigmoid_fast(g.y));
+              }
+              const __nv_bfloat162 x2 = __floats2bfloat162_rn(__uint_as_float(o[v4 * 8 + 2 * e]) * inv,
+                                                              __uint_as_float(o[v4 * 8 + 2 * e + 1]) * inv);
+              const __nv_bfloat162 r2 = __hmul2(x2, g2);
+              w[e] = *reinterpret_cast<const uint32_t*>(&r2);
             }
           } else {
 #pragma unroll
