@@ -271,6 +271,14 @@ __global__ void __launch_bounds__(192, 1)
     const uint8_t* mrow = a.key_mask ? a.key_mask + static_cast<long long>(b) * a.S : nullptr;
     const bool flags = a.softcap > 0.f || a.window > 0;
     bool ok = true;
+    uint4 mnext[4];  // key-mask bytes of the next tile, in flight while the current one is processed
+    auto load_mask = [&](int kk) {
+#pragma unroll
+      for (int v4 = 0; v4 < 4; ++v4)
+        mnext[v4] = (mrow && a.mask_vec && kk + 16 * v4 < a.S) ? *reinterpret_cast<const uint4*>(mrow + kk + 16 * v4)
+                                                                 : make_uint4(0, 0, 0, 0);
+    };
+    load_mask(kb_lo * BK);
     for (int t = 0; t < n; ++t) {
       const int s = t & 1;
       const uint32_t ph = (t >> 1) & 1;
@@ -284,13 +292,16 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (mrow) {
         if (a.mask_vec) {
+          // this tile's mask bytes were loaded during the previous tile; start
+          // the next tile's loads now so their latency overlaps this tile
           uint32_t all = 0x01010101u;
           uint4 w[4];
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
-            w[v4] = (k0 + 16 * v4 < a.S) ? *reinterpret_cast<const uint4*>(mrow + k0 + 16 * v4) : make_uint4(0, 0, 0, 0);
+            w[v4] = mnext[v4];
             all &= w[v4].x & w[v4].y & w[v4].z & w[v4].w;
           }
+          load_mask(k0 + BK);
           if (all != 0x01010101u) {  // some key masked: build the bits (0/1 bytes)
             uint32_t bits[2] = {0u, 0u};
 #pragma unroll
