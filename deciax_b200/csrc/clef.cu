@@ -326,7 +326,7 @@ struct QkvFusion {
 // Whether the QKV projection can carry the fused epilogue: every 256-column
 // tile must hold whole heads and the rotated half must be whole 32-column chunks.
 static bool qkv_fusable(int head_dim, int rot) {
-  return (head_dim == 64 || head_dim == 128 || head_dim == 256) && rot % 64 == 0;
+  return (head_dim == 64 || head_dim == 128 || head_dim == 256) && (rot % 64 == 0 || rot == 32);
 }
 
 static void gemm_bf16_qkv(Launcher& L, const bf16* A, int lda, const bf16* B, int ldb, int M, int N, int K, bf16* out,
@@ -334,7 +334,8 @@ static void gemm_bf16_qkv(Launcher& L, const bf16* A, int lda, const bf16* B, in
   REQUIRE(M > 0 && N > 0 && K > 0, "GEMM dimensions must be positive");
   REQUIRE(K % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 && ldo % 8 == 0, "bf16 GEMM needs strides multiple of 8");
   REQUIRE(aligned16(A) && aligned16(B) && aligned16(out), "bf16 GEMM operands must be 16-byte aligned");
-  REQUIRE(qkv_fusable(f.head_dim, f.rot), "fused QKV epilogue needs head_dim in {64,128,256} and rot % 64 == 0");
+  REQUIRE(qkv_fusable(f.head_dim, f.rot),
+          "fused QKV epilogue needs head_dim in {64,128,256} and a rotary dimension of 32 or a multiple of 64");
   REQUIRE(N == f.hq * 2 * f.head_dim + 2 * f.hkv * f.head_dim, "fused QKV epilogue: N does not match the heads");
   GemmArgs args{M, N, K, out, ldo, nullptr, nullptr, 0, L.status, f.q_norm, f.k_norm, f.rope_cos, f.rope_sin,
                 f.hq, f.hkv, f.head_dim, f.rot, f.seq, f.eps};

@@ -157,7 +157,7 @@ __device__ __forceinline__ void qkv_epilogue(const GemmArgs& a, uint32_t taddr, 
     const bf* w = is_k ? a.k_norm : a.q_norm;
 #pragma unroll 1
     for (int c = 0; c < d; c += 32) {
-      if (c >= half && c < a.rot) continue;  // written together with its rotate-half partner
+      if (half >= 32 && c >= half && c < a.rot) continue;  // written together with its rotate-half partner
       uint32_t ra[32];
       float wa[32], ya[32];
       __syncwarp();
@@ -166,7 +166,25 @@ __device__ __forceinline__ void qkv_epilogue(const GemmArgs& a, uint32_t taddr, 
       load32_bf16(w + c, wa);
 #pragma unroll
       for (int j = 0; j < 32; ++j) ya[j] = round_to<bf>(round_to<bf>(__uint_as_float(ra[j])) * rs * (wa[j] + 1.f));
-      if (c < half) {
+      if (half == 16 && c == 0) {  // rot = 32: both rotate-half partners lie in this chunk
+        float cs[16], sn[16];
+        const float4* cp = reinterpret_cast<const float4*>(a.rope_cos + static_cast<size_t>(pos) * 16);
+        const float4* sp = reinterpret_cast<const float4*>(a.rope_sin + static_cast<size_t>(pos) * 16);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 c4 = cp[v], s4 = sp[v];
+          cs[4 * v] = c4.x, cs[4 * v + 1] = c4.y, cs[4 * v + 2] = c4.z, cs[4 * v + 3] = c4.w;
+          sn[4 * v] = s4.x, sn[4 * v + 1] = s4.y, sn[4 * v + 2] = s4.z, sn[4 * v + 3] = s4.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float co = round_to<bf>(cs[j]), si = round_to<bf>(sn[j]);
+          const float lo = round_to<bf>(round_to<bf>(ya[j] * co) + round_to<bf>(-ya[j + 16] * si));
+          const float hi = round_to<bf>(round_to<bf>(ya[j + 16] * co) + round_to<bf>(ya[j] * si));
+          ya[j] = lo;
+          ya[j + 16] = hi;
+        }
+      } else if (c < half) {
         uint32_t rb[32];
         float wb[32], yb[32], cs[32], sn[32];
         tmem_ld32(taddr + seg + c + half, rb);

@@ -190,7 +190,7 @@ int clef_op_gemm(int dtype, int epi, int M, int N, int K, const void* A, const v
  * key head leave RMSNorm(1+w)-normalised with partial RoPE at positions
  * row % seq (models/qwen3_5/text.py:79-88), each gate leaves as
  * T(sigmoid(T(gate))) (text.py:91) and v is unchanged.  Needs d in
- * {64, 128, 256} and d * partial_rotary_factor a multiple of 64. */
+ * {64, 128, 256} and d * partial_rotary_factor equal to 32 or a multiple of 64. */
 int clef_op_gemm_qkv(const void* A, const void* B, void* out, int M, int K, int hq, int hkv, int d,
                      float partial_rotary_factor, float rope_theta, int seq, const void* q_norm, const void* k_norm,
                      float eps, void* stream);

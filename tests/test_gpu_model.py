@@ -43,6 +43,13 @@ FLASH = TextConfig.full_attention(
     vocab_size=300, partial_rotary_factor=0.25,
 )
 
+# head_dim 128 with partial rotary 0.25 (rot 32, the 27B-shaped config): the fused QKV epilogue's
+# in-chunk rotate-half path
+D128 = TextConfig.full_attention(
+    hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2, head_dim=128, num_layers=2,
+    vocab_size=300, partial_rotary_factor=0.25,
+)
+
 SPECS = {
     "ragged": BatchSpec(states=3, seq=256, questions=2, options_per_question=3, lengths=(256, 130, 40), row_bucket=4),
     "full": BatchSpec(states=2, seq=128, questions=4, options_per_question=4),
@@ -62,7 +69,7 @@ def oracle_forward(weights, arrays, config, head, dtype, flags=KernelFlags()):
                      embed_scale=flags.embed_scale, return_hidden=True)
 
 
-@pytest.mark.parametrize("config", [SMALL, WIDE, FLASH], ids=["d64", "d256", "d256-prf025"])
+@pytest.mark.parametrize("config", [SMALL, WIDE, FLASH, D128], ids=["d64", "d256", "d256-prf025", "d128-prf025"])
 @pytest.mark.parametrize("spec", list(SPECS), ids=list(SPECS))
 def test_forward_fp32_matches_oracle(config, spec):
     model, weights = build(config, SMALL_HEAD, "fp32")
@@ -77,7 +84,7 @@ def test_forward_fp32_matches_oracle(config, spec):
     assert (logits[~m] == -1e9).all()
 
 
-@pytest.mark.parametrize("config", [SMALL, WIDE, FLASH], ids=["d64", "d256", "d256-prf025"])
+@pytest.mark.parametrize("config", [SMALL, WIDE, FLASH, D128], ids=["d64", "d256", "d256-prf025", "d128-prf025"])
 @pytest.mark.parametrize("spec", list(SPECS), ids=list(SPECS))
 def test_forward_bf16_probabilities(config, spec):
     model, weights = build(config, SMALL_HEAD, "bf16")

@@ -125,7 +125,8 @@ def test_gemm_bf16_swiglu_epilogue(m, f, k):
     np.testing.assert_allclose(host(out), expected, rtol=2 * BF16_RTOL, atol=2e-3)
 
 
-@pytest.mark.parametrize("d,prf,hq,hkv", [(256, 0.25, 2, 1), (128, 0.5, 4, 2), (64, 1.0, 4, 2), (256, 1.0, 1, 1)])
+@pytest.mark.parametrize("d,prf,hq,hkv", [(256, 0.25, 2, 1), (128, 0.5, 4, 2), (64, 1.0, 4, 2), (256, 1.0, 1, 1),
+                                          (128, 0.25, 4, 2), (64, 0.5, 2, 2)])
 def test_gemm_qkv_fused_epilogue(d, prf, hq, hkv):
     """QKV GEMM + q/k RMSNorm + partial RoPE + sigmoid(gate) in the epilogue vs the oracle."""
     import torch
