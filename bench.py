@@ -71,6 +71,32 @@ def algorithmic_flops(c, lengths) -> tuple[float, float, float]:
     return linear, attention, 2.0 * D * 2 * F
 
 
+def rank_reduce(value: float, op: str = "max") -> float:
+    """``value`` reduced over the ranks of the default process group ("max" or
+    "sum"; the value itself without one).  On the group's own device: CUDA
+    for NCCL, the host for gloo."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return value
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def share_from_rank0(make):
+    """The object rank 0 builds with ``make()`` (e.g. an NCCL unique id), on every rank."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return make()
+    obj = [make() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -338,15 +364,8 @@ def gpu_arm(args) -> None:
     barrier()
     decisions = sum(len(f) for f in field_probabilities(logits, arrays))
 
-    def max_over_ranks(v: float) -> float:
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    elapsed_ms = max_over_ranks(elapsed_ms)
-    e2e_s = max_over_ranks(e2e_s)
+    elapsed_ms = rank_reduce(elapsed_ms, "max")
+    e2e_s = rank_reduce(e2e_s, "max")
     tokens = STATES * SEQ
     value = world * tokens * args.steps / (elapsed_ms / 1e3)
     e2e_value = world * tokens * args.steps / e2e_s
@@ -601,12 +620,7 @@ def serving_arm(args) -> None:
         long_t.append(t)
     assert all(len(a["answers"]) == QUESTIONS for a in answers)
 
-    def agg(v: float, op: str) -> float:
-        if not dist:
-            return v
-        x = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(x, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
-        return float(x.item())
+    agg = rank_reduce
 
     def pct(vals, q):
         return float(np.percentile(np.asarray(vals) * 1e3, q)) if vals else 0.0
@@ -732,13 +746,12 @@ def cfg4_arm(args) -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
-        obj = [None]
-        if rank == 0:
+        def make_id() -> bytes:
             buf = ct.create_string_buffer(_lib.NCCL_ID_BYTES)
             _lib.check(_lib.load().clef_nccl_unique_id(buf))
-            obj = [buf.raw]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
+            return buf.raw
+
+        nccl_id = share_from_rank0(make_id)
     c = CFG4_BATCH
     model = build_model(local, max_seq_len=c["seq"], cfg=CFG4, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     arrays = collate(mixed_records(c["states"], c["seq"], CFG4["vocab_size"], seed=31), 0)
@@ -774,10 +787,7 @@ def cfg4_arm(args) -> None:
     logits = out.cpu().numpy()
     if not np.isfinite(logits[arrays["option_mask"]]).all():
         raise SystemExit("non-finite logits")
-    if dist:
-        x = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        ms = float(x.item())
+    ms = rank_reduce(ms, "max")
     tokens = c["states"] * c["seq"]
     linear, attention, _ = algorithmic_flops(CFG4, [c["seq"]] * c["states"])
     flops = linear + attention
