@@ -70,6 +70,7 @@ class ClefConfigC(ctypes.Structure):
         ("linear_key_head_dim", ctypes.c_int32),
         ("linear_value_head_dim", ctypes.c_int32),
         ("linear_conv_kernel_dim", ctypes.c_int32),
+        ("tp_timeout_ms", ctypes.c_int32),
     ]
 
 

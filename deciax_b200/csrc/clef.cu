@@ -19,6 +19,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -28,6 +29,7 @@
 #include <set>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/clef_b200.h"
@@ -647,6 +649,8 @@ struct Model {
   std::string last_error;
   cudaStream_t stream = nullptr;
   ncclComm_t comm = nullptr;
+  int tp_timeout_ms = 0;  // longest host wait for the other TP ranks, 0 = no limit
+  bool broken = false;    // a TP wait ran out: a collective may still wait on the stream
   DBuf status;  // int
   DBuf embedding, lm_head, final_norm, rope_cos, rope_sin;
   std::set<std::string> top_have;
@@ -695,6 +699,89 @@ struct Model {
     p2p = false;
   }
 
+  // Milliseconds since t0.
+  static double since_ms(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  }
+
+  // The communicator is non-blocking, so that a rank that never joins cannot
+  // hold this one forever: a call may return ncclInProgress while NCCL sets
+  // up (or enqueues) in the background.  Poll until it is done, so that the
+  // work enqueued after it stays ordered behind it, or until tp_timeout_ms.
+  void nccl_done(ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return;
+    if (r != ncclInProgress) throw Error(CLEF_ENCCL, std::string(what) + ": " + ncclGetErrorString(r));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+      ncclResult_t st = ncclInProgress;
+      const ncclResult_t q = ncclCommGetAsyncError(comm, &st);
+      if (q != ncclSuccess) st = q;
+      if (st == ncclSuccess) return;
+      if (st != ncclInProgress) {
+        broken = true;
+        throw Error(CLEF_ENCCL, std::string(what) + ": " + ncclGetErrorString(st));
+      }
+      if (tp_timeout_ms > 0 && since_ms(t0) > tp_timeout_ms) {
+        broken = true;
+        throw Error(CLEF_ENCCL, std::string(what) + ": the other tensor-parallel ranks did not take part within " +
+                                    std::to_string(tp_timeout_ms) + " ms");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+  }
+
+  // Create the TP communicator (non-blocking).  If not every rank joins
+  // within tp_timeout_ms the half-made communicator is aborted -- nothing of
+  // it is on a stream yet -- and the call fails with CLEF_ENCCL.
+  void create_comm(const ncclUniqueId& id) {
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = ncclCommInitRankConfig(&comm, tp, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+      if (comm) ncclCommAbort(comm);
+      comm = nullptr;
+      throw Error(CLEF_ENCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+    }
+    try {
+      nccl_done(r, "ncclCommInitRankConfig");
+    } catch (const Error& e) {
+      ncclCommAbort(comm);
+      comm = nullptr;
+      broken = false;
+      throw Error(CLEF_ENCCL, std::string("tensor-parallel communicator of ") + std::to_string(tp) +
+                                  " ranks not formed (rank " + std::to_string(rank) + "): " + e.what());
+    }
+  }
+
+  // Host wait for the forward on `stream`.  With TP and a deadline, poll the
+  // stream instead of blocking in it: a rank that skipped its forward leaves
+  // this rank's collective waiting, and the caller gets CLEF_ENCCL instead of
+  // a hang.  The handle is then unusable (the collective still waits on the
+  // stream; only the end of the process releases it).
+  void wait_stream() {
+    if (tp <= 1 || tp_timeout_ms <= 0) {
+      CUDA_CHECK(cudaStreamSynchronize(stream));
+      return;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+      const cudaError_t e = cudaStreamQuery(stream);
+      if (e == cudaSuccess) return;
+      if (e != cudaErrorNotReady) CUDA_CHECK(e);
+      ncclResult_t st = ncclSuccess;
+      if (ncclCommGetAsyncError(comm, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress) {
+        broken = true;
+        throw Error(CLEF_ENCCL, std::string("tensor-parallel collective failed: ") + ncclGetErrorString(st));
+      }
+      if (since_ms(t0) > tp_timeout_ms) {
+        broken = true;
+        throw Error(CLEF_ENCCL, "tensor-parallel forward did not finish within " + std::to_string(tp_timeout_ms) +
+                                    " ms: another rank did not take part in a collective; this handle is unusable");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+  }
+
   // Collective over the TP group: all ranks call it with the same buffer sizes.
   void exchange_ipc() {
     close_peers();
@@ -705,10 +792,10 @@ struct Model {
     ipc_scratch.ensure(static_cast<size_t>(tp) * hb);
     uint8_t* d = ipc_scratch.as<uint8_t>();
     CUDA_CHECK(cudaMemcpyAsync(d + rank * hb, h, hb, cudaMemcpyHostToDevice, stream));
-    NCCL_CHECK(ncclAllGather(d + rank * hb, d, hb, ncclUint8, comm, stream));
+    nccl_done(ncclAllGather(d + rank * hb, d, hb, ncclUint8, comm, stream), "ncclAllGather");
     std::vector<uint8_t> all(static_cast<size_t>(tp) * hb);
     CUDA_CHECK(cudaMemcpyAsync(all.data(), d, all.size(), cudaMemcpyDeviceToHost, stream));
-    CUDA_CHECK(cudaStreamSynchronize(stream));
+    wait_stream();
     for (int k = 0; k < tp; ++k) {
       if (k == rank) {
         peer_part[k] = ws.partial.p;
@@ -727,12 +814,34 @@ struct Model {
 
   // Every rank of the TP group has reached this point of its stream.
   void tp_barrier(Launcher& Lc) {
-    NCCL_CHECK(ncclAllReduce(barrier_buf.p, barrier_buf.p, 1, ncclFloat32, ncclSum, comm, Lc.stream));
+    nccl_done(ncclAllReduce(barrier_buf.p, barrier_buf.p, 1, ncclFloat32, ncclSum, comm, Lc.stream), "ncclAllReduce");
   }
 
   ~Model() {
     if (tp > 1) close_peers();
-    if (comm) ncclCommDestroy(comm);
+    if (comm) {
+      // non-blocking communicator: flush, wait (bounded by tp_timeout_ms), free;
+      // abort it instead if it does not quiesce in time
+      const ncclResult_t r = ncclCommFinalize(comm);
+      bool done = r == ncclSuccess;
+      if (r == ncclInProgress) {
+        const auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+          ncclResult_t st = ncclInProgress;
+          if (ncclCommGetAsyncError(comm, &st) != ncclSuccess) break;
+          if (st != ncclInProgress) {
+            done = st == ncclSuccess;
+            break;
+          }
+          if (tp_timeout_ms > 0 && since_ms(t0) > tp_timeout_ms) break;
+          std::this_thread::sleep_for(std::chrono::microseconds(100));
+        }
+      }
+      if (done)
+        ncclCommDestroy(comm);
+      else
+        ncclCommAbort(comm);
+    }
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -749,6 +858,7 @@ struct Model {
     device = dev;
     rank = tp_rank;
     tp = tp_size;
+    tp_timeout_ms = c.tp_timeout_ms > 0 ? c.tp_timeout_ms : 0;
     dtype = dt;
     esz = dt == CLEF_DTYPE_BF16 ? 2 : 4;
     D = c.hidden_size;
@@ -818,7 +928,7 @@ struct Model {
       REQUIRE(nccl_id != nullptr, "tp > 1 needs an NCCL unique id");
       ncclUniqueId id;
       std::memcpy(&id, nccl_id, sizeof(id));
-      NCCL_CHECK(ncclCommInitRank(&comm, tp, id, rank));
+      create_comm(id);
       barrier_buf.alloc(256);
       CUDA_CHECK(cudaMemset(barrier_buf.p, 0, 256));
     }
@@ -1544,7 +1654,8 @@ struct Model {
       Lc.cat = saved;
       return;
     }
-    NCCL_CHECK(ncclAllReduce(part, part, static_cast<size_t>(Tt) * D, ncclFloat32, ncclSum, comm, Lc.stream));
+    nccl_done(ncclAllReduce(part, part, static_cast<size_t>(Tt) * D, ncclFloat32, ncclSum, comm, Lc.stream),
+              "ncclAllReduce");
     Lc.mark(kCatAllReduce);
     const long long n = static_cast<long long>(Tt) * D;
     residual_add_f32_kernel<T><<<static_cast<int>(std::min<long long>((n + 255) / 256, 8192)), 256, 0, Lc.stream>>>(
@@ -1775,7 +1886,7 @@ struct Model {
       hid.resize(nh * esz);
       CUDA_CHECK(cudaMemcpyAsync(hid.data(), w.h.p, nh * esz, cudaMemcpyDeviceToHost, stream));
     }
-    CUDA_CHECK(cudaStreamSynchronize(stream));
+    wait_stream();
     check_status();
     std::memcpy(out_logits, tmp_logits.data(), nlog * 4);
     if (out_hidden) {
@@ -1838,6 +1949,11 @@ using clef::Model;
 
 template <typename F>
 static int guarded(Model* m, F&& f) {
+  if (m && m->broken) {
+    m->last_error = "handle unusable after a tensor-parallel timeout or NCCL failure; destroy it and end the process";
+    clef::set_global_error(m->last_error);
+    return CLEF_ESTATE;
+  }
   try {
     f();
     return CLEF_OK;
@@ -1978,6 +2094,10 @@ int clef_last_launch_count(void* handle) {
 int clef_destroy(void* handle) {
   Model* m = static_cast<Model*>(handle);
   return guarded(nullptr, [&] {
+    // After a TP timeout a collective may still wait on the stream: freeing
+    // its buffers or destroying its communicator would block behind it (or
+    // pull memory from under it), so the model is left for the process exit.
+    if (m && m->broken) return;
     if (m) {
       cudaSetDevice(m->device);
       if (m->ws.host_pinned.p) {

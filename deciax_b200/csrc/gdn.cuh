@@ -54,7 +54,7 @@ struct GdnShape {
   static constexpr int NC = DH / TCOL;                           // columns per thread
   static constexpr int RM = C / TROW;                            // rows per thread, 64-row outputs
   static constexpr int RS = DH / TROW > 0 ? DH / TROW : 1;       // rows per thread, DH-row state
-  static constexpr size_t floats = size_t(DH) * DH + 3 * C * LDQ + C * DH + C * LDA + 4 * C;
+  static constexpr size_t floats = size_t(DH) * DH + 3 * C * LDQ + C * DH + C * LDA + 4 * C + 3 * DH * 4;
   static constexpr size_t bytes = floats * 4;
 };
 
@@ -118,57 +118,82 @@ __device__ __forceinline__ float group_sum(float x) {
 // before the arithmetic.  The taps are right-aligned in W slots (zero weights
 // first), so each output is 0 + x_0 w_0 + ... in the reference's order.
 template <typename T, int DH, int W>
-__device__ __forceinline__ void gdn_load_chunk(const GdnArgs& a, const T* proj, const T* convw, long long row0, int t0,
-                                               int q_col, int k_col, int v_col, float* Qs, float* Ks, float* Vs) {
+__device__ __forceinline__ void gdn_load_chunk(const GdnArgs& a, const T* proj, const T* convw, const float* wsm,
+                                               long long row0, int t0, int q_col, int k_col, int v_col, float* Qs,
+                                               float* Ks, float* Vs) {
   constexpr int C = kGdnChunk, LDQ = GdnShape<DH>::LDQ, VN = GdnVec<T>::N, GL = DH / VN, RPP = kGdnThreads / GL;
-  constexpr int RT = C / RPP > 0 ? C / RPP : 1;
+  constexpr int RT = C / RPP > 0 ? C / RPP : 1, NX = RT + W - 1;
   const int tid = threadIdx.x, g = tid % GL, r0 = (tid / GL) * RT;
   const int shift = W - a.width;
-#pragma unroll 1
+  if (r0 >= C) return;  // warp-uniform: RT * (32 / GL) divides 64
+  // conv width <= 4: every tap row of q, k and v in flight before any
+  // arithmetic; wider convs load one kind at a time (register budget)
+  constexpr int NK = W <= 4 ? 3 : 1;
+  uint4 raw[NK][NX];
+  auto load_kind = [&](int kind, uint4 (&dst)[NX]) {
+    const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + g * VN;
+#pragma unroll
+    for (int i = 0; i < NX; ++i) {
+      const int tt = t0 + r0 - (W - 1) + i;
+      dst[i] = (tt >= 0 && tt < a.S) ? *reinterpret_cast<const uint4*>(proj + (row0 + tt) * a.ldp + col)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  if constexpr (NK == 3) {
+#pragma unroll
+    for (int kind = 0; kind < 3; ++kind) load_kind(kind, raw[kind]);
+  }
+#pragma unroll
   for (int kind = 0; kind < 3; ++kind) {
     const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + g * VN;
+    if constexpr (NK == 1) load_kind(kind, raw[0]);
+    const uint4 (&rk)[NX] = raw[NK == 3 ? kind : 0];
     float w[VN][W];
 #pragma unroll
     for (int c = 0; c < VN; ++c)
 #pragma unroll
       for (int i = 0; i < W; ++i)
-        w[c][i] = i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f;
+        w[c][i] = wsm ? wsm[(kind * DH + g * VN + c) * W + i]
+                      : (i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f);
+    GdnVec<T> x[NX];
+#pragma unroll
+    for (int i = 0; i < NX; ++i) {
+      if constexpr (sizeof(T) == 2) {
+        const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&rk[i]);
+#pragma unroll
+        for (int c = 0; c < VN; ++c) x[i].v[c] = __bfloat162float(hv[c]);
+      } else {
+        const float* fv = reinterpret_cast<const float*>(&rk[i]);
+#pragma unroll
+        for (int c = 0; c < VN; ++c) x[i].v[c] = fv[c];
+      }
+    }
     float* dst = kind == 0 ? Qs : kind == 1 ? Ks : Vs;
     const int ld = kind == 2 ? DH : LDQ;
-    if (r0 < C) {  // warp-uniform: RT * (32 / GL) divides 64
-      GdnVec<T> x[RT + W - 1];
 #pragma unroll
-      for (int i = 0; i < RT + W - 1; ++i) {
-        const int tt = t0 + r0 - (W - 1) + i;
-        if (tt >= 0 && tt < a.S)
-          x[i].load(proj + (row0 + tt) * a.ldp + col);
-        else
-          x[i].zero();
+    for (int j = 0; j < RT; ++j) {
+      const int r = r0 + j;
+      GdnVec<T> y;
+#pragma unroll
+      for (int c = 0; c < VN; ++c) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(x[j + i].v[c], w[c][i]));
+        const float z = round_to<T>(acc);
+        y.v[c] = t0 + r < a.S ? round_to<T>(z * sigmoid_fast(z)) : 0.f;
+      }
+      if (kind < 2) {
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < VN; ++c) ss += y.v[c] * y.v[c];
+        const float inv = rsqrtf(group_sum<GL>(ss) + 1e-6f);
+        const float scale = kind == 0 ? a.qscale : 1.f;
+#pragma unroll
+        for (int c = 0; c < VN; ++c) y.v[c] = round_to<T>(y.v[c] * inv) * scale;
       }
 #pragma unroll
-      for (int j = 0; j < RT; ++j) {
-        const int r = r0 + j;
-        GdnVec<T> y;
-#pragma unroll
-        for (int c = 0; c < VN; ++c) {
-          float acc = 0.f;
-#pragma unroll
-          for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(x[j + i].v[c], w[c][i]));
-          const float z = round_to<T>(acc);
-          y.v[c] = t0 + r < a.S ? round_to<T>(z * sigmoid_fast(z)) : 0.f;
-        }
-        if (kind < 2) {
-          float ss = 0.f;
-#pragma unroll
-          for (int c = 0; c < VN; ++c) ss += y.v[c] * y.v[c];
-          const float inv = rsqrtf(group_sum<GL>(ss) + 1e-6f);
-          const float scale = kind == 0 ? a.qscale : 1.f;
-#pragma unroll
-          for (int c = 0; c < VN; ++c) y.v[c] = round_to<T>(y.v[c] * inv) * scale;
-        }
-#pragma unroll
-        for (int c = 0; c < VN; ++c) dst[r * ld + g * VN + c] = y.v[c];
-      }
+      for (int c = 0; c < VN; c += 4)
+        *reinterpret_cast<float4*>(dst + r * ld + g * VN + c) = make_float4(y.v[c], y.v[c + 1], y.v[c + 2], y.v[c + 3]);
     }
   }
 }
@@ -275,6 +300,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chunk_kernel(GdnArgs a) {
   float* bs = gs + C;        // beta
   float* es = bs + C;        // e^g
   float* ws = es + C;        // e^(g_last - g)
+  float* wconv = ws + C;     // [3][DH][4] this head's q / k / v conv taps, right-aligned (width <= 4)
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -291,6 +317,15 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chunk_kernel(GdnArgs a) {
   const int tr = tid / TCOL, tc = tid % TCOL;        // 64xDH and DHxDH products
 
   for (int i = tid; i < DH * DH; i += kGdnThreads) St[i] = 0.f;
+  if (a.width <= 4) {
+    const int shift = 4 - a.width;
+    for (int i = tid; i < 3 * DH * 4; i += kGdnThreads) {
+      const int kind = i / (DH * 4), c = (i / 4) % DH, tap = i % 4;
+      const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + c;
+      wconv[i] = tap >= shift ? to_f32(convw[static_cast<long long>(col) * a.width + (tap - shift)]) : 0.f;
+    }
+  }
+  __syncthreads();
   GdnVec<T> nwv;  // this thread's slice of the gated norm's weight
   nwv.load(nw + (tid % (DH / GdnVec<T>::N)) * GdnVec<T>::N);
 
@@ -300,9 +335,9 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chunk_kernel(GdnArgs a) {
     // 1. conv + SiLU, L2 norms, gates
     {
       if (a.width <= 4)
-        gdn_load_chunk<T, DH, 4>(a, proj, convw, row0, t0, q_col, k_col, v_col, Qs, Ks, Vs);
+        gdn_load_chunk<T, DH, 4>(a, proj, convw, wconv, row0, t0, q_col, k_col, v_col, Qs, Ks, Vs);
       else
-        gdn_load_chunk<T, DH, 8>(a, proj, convw, row0, t0, q_col, k_col, v_col, Qs, Ks, Vs);
+        gdn_load_chunk<T, DH, 8>(a, proj, convw, nullptr, row0, t0, q_col, k_col, v_col, Qs, Ks, Vs);
       if (tid < C) {
         const int t = t0 + tid;
         if (t < a.S) {

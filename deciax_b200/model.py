@@ -80,7 +80,13 @@ class ClefCudaModel:
         name: str = "clef",
         tokenizer: Any = None,
         pad_token_id: int = 0,
+        tp_timeout: float = 300.0,
+        heartbeat: Any = None,
     ) -> None:
+        """``tp_timeout`` (seconds, 0 = no limit) bounds the library's host
+        waits for the other TP ranks: communicator creation and each host
+        forward.  ``heartbeat`` (a ``TpHeartbeat``) makes each forward check
+        in with the other ranks before launching anything."""
         if dtype not in ("bf16", "fp32"):
             raise ValueError("Clef CUDA dtype must be 'bf16' or 'fp32'")
         if not config.vocab_size:
@@ -92,6 +98,7 @@ class ClefCudaModel:
         self.device = device
         self.tokenizer = tokenizer
         self.pad_token_id = pad_token_id
+        self.heartbeat = heartbeat
         # records are encoded so that their sequence bucket fits the library's max_seq_len
         fits = [b for b in SEQUENCE_BUCKETS if b <= max_seq_len]
         self.max_token_budget = fits[-1] if fits else max_seq_len
@@ -128,6 +135,7 @@ class ClefCudaModel:
             linear_key_head_dim=config.linear_key_head_dim,
             linear_value_head_dim=config.linear_value_head_dim,
             linear_conv_kernel_dim=config.linear_conv_kernel_dim,
+            tp_timeout_ms=int(round(tp_timeout * 1000)),
         )
         handle = ctypes.c_void_p()
         dt = _lib.DTYPE_BF16 if dtype == "bf16" else _lib.DTYPE_F32
@@ -267,12 +275,26 @@ class ClefCudaModel:
 
     def _forward(self, arrays: Mapping[str, Any], hidden: bool) -> tuple[np.ndarray, np.ndarray | None]:
         keep: list = []
-        c = batch_struct(arrays, keep)
+        try:
+            c = batch_struct(arrays, keep)
+        except Exception as e:
+            self.report_failure(e)
+            raise
         out = np.empty((c.b, c.o), np.float32)
         hid = np.empty((c.b, c.s, self.config.hidden_size), np.float32) if hidden else None
+        if self.heartbeat is not None:
+            self.heartbeat.arrive()
         status = self._lib.clef_forward(self._handle, ctypes.byref(c), out.ctypes.data, hid.ctypes.data if hid is not None else None)
+        if status != _lib.CLEF_OK:
+            self.report_failure(RuntimeError(f"clef_forward status {status}"))
         _lib.check(status, self._handle)
         return out, hid
+
+    def report_failure(self, e: BaseException) -> None:
+        """Tell the other TP ranks (through the heartbeat) that this rank's
+        next forward will not come."""
+        if self.heartbeat is not None:
+            self.heartbeat.fail(f"{type(e).__name__}: {e}")
 
     def forward_device(self, tensors: Mapping[str, Any], out: Any, stream: int | None = None) -> None:
         """Enqueue a forward over device-resident tensors (torch CUDA tensors:
@@ -284,6 +306,8 @@ class ClefCudaModel:
         )
         for key in _lib.BATCH_KEYS:
             setattr(c, key, tensors[key].data_ptr())
+        if self.heartbeat is not None:
+            self.heartbeat.arrive()
         status = self._lib.clef_forward_device(self._handle, ctypes.byref(c), out.data_ptr(), stream)
         _lib.check(status, self._handle)
 

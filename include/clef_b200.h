@@ -75,6 +75,14 @@ typedef struct ClefConfig {
   int32_t linear_key_head_dim;   /* must equal linear_value_head_dim, one of 8, 16, 32, 64, 128 */
   int32_t linear_value_head_dim;
   int32_t linear_conv_kernel_dim; /* depthwise causal conv width, 1..8 */
+  /* Tensor parallelism only: the longest host wait, in milliseconds, for the
+   * other ranks -- communicator creation and each clef_forward.  0 = no limit.
+   * A rank that never joins makes clef_create fail with CLEF_ENCCL (the
+   * communicator is aborted); a forward that does not finish in time returns
+   * CLEF_ENCCL and leaves the handle unusable (CLEF_ESTATE on every later
+   * call; clef_destroy then releases nothing on the device, since a collective
+   * may still be waiting on the stream -- end the process). */
+  int32_t tp_timeout_ms;
 } ClefConfig;
 
 /* One collated batch: the dict returned by the reference collate()
