@@ -504,9 +504,10 @@ def gemm_arm(args) -> None:
 
 
 def attention_arm(args) -> None:
-    """cfg2's attention layer alone: causal GQA over a packed projection of
-    8 x 2048 tokens, 16 query / 8 key-value heads of 256, with the sigmoid
-    gate, through clef_op_attention; TFLOP/s counts causal pairs only."""
+    """One attention layer alone: causal GQA over a packed projection with the
+    sigmoid gate, through clef_op_attention; TFLOP/s counts causal pairs only.
+    ``attention``: cfg2's layer (8 x 2048 tokens, 16 query / 8 key-value heads
+    of 256); ``attention4``: cfg4's (16 x 8192 tokens, 32 / 16 heads of 128)."""
     import torch
 
     from deciax_b200 import _lib
@@ -517,7 +518,12 @@ def attention_arm(args) -> None:
     torch.cuda.set_device(0)
     gen = torch.Generator(device="cuda:0")
     gen.manual_seed(3)
-    B, S, H, HK, Dh = STATES, SEQ, CFG2["num_attention_heads"], CFG2["num_key_value_heads"], CFG2["head_dim"]
+    if args.workload == "attention4":
+        B, S, H, HK, Dh = CFG4_BATCH["states"], CFG4_BATCH["seq"], CFG4["num_attention_heads"], CFG4["num_key_value_heads"], CFG4["head_dim"]
+        label = "cfg4 attention layer throughput (B16 S8192 32q/16kv x128, causal, gated)"
+    else:
+        B, S, H, HK, Dh = STATES, SEQ, CFG2["num_attention_heads"], CFG2["num_key_value_heads"], CFG2["head_dim"]
+        label = "cfg2 attention layer throughput (B8 S2048 16q/8kv x256, causal, gated)"
     n = H * 2 * Dh + 2 * HK * Dh
     qkv = torch.empty((B * S, n), dtype=torch.bfloat16, device="cuda").normal_(0.0, 1.0, generator=gen)
     mask = torch.ones((B, S), dtype=torch.uint8, device="cuda")
@@ -541,7 +547,7 @@ def attention_arm(args) -> None:
     ms = start.elapsed_time(end) / args.steps
     flops = 2.0 * H * Dh * S * (S + 1) * B
     peaks = measured_peaks()
-    print(json.dumps({"metric": "cfg2 attention layer throughput (B8 S2048 16q/8kv x256, causal, gated)",
+    print(json.dumps({"metric": label,
                       "value": flops / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps,
                       "warmup": args.warmup, "frac_of_measured_burst": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
                       "dtype": "bf16", "data": "synthetic", "gpu_launches": args.steps}), flush=True)
@@ -901,7 +907,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg4", "cfg5", "attention", "gdn", "rmsnorm"), default="cfg2",
+    ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg4", "cfg5", "attention", "attention4", "gdn", "rmsnorm"), default="cfg2",
                     help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark; "
                     "cfg5 = the serving sweep through ClefEngine; attention = cfg2's attention layer alone; "
                     "gdn = one Gated DeltaNet core; rmsnorm = cfg2's RMSNorm alone; cfg4 = the 27B-shaped model, "
@@ -911,7 +917,7 @@ def main() -> None:
         reference_arm(args)
     elif args.workload == "cfg3":
         gemm_arm(args)
-    elif args.workload == "attention":
+    elif args.workload in ("attention", "attention4"):
         attention_arm(args)
     elif args.workload == "gdn":
         gdn_arm(args)

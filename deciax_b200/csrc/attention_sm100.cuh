@@ -6,13 +6,20 @@
 //   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M=128, N=64,
 //               K=D) into one of two TMEM S buffers, then O += P_{j-1} V_{j-1}
 //               (M=128, N=D, K=64) into the TMEM O accumulator.  V is the
-//               MN-major B operand (it is stored [keys][d]).
+//               MN-major B operand (it is stored [keys][d]).  For D = 128, P
+//               is the A operand straight from tensor memory (see below).
 //   warps 2..5  softmax: thread r owns query row r.  It reads its S row from
 //               TMEM, masks (key mask, causal, optional window/softcap) with
 //               MASK_FILL = -1e30, keeps a running max / sum, writes
 //               P = exp(s - m) as bf16 into swizzled shared memory for the
 //               P.V MMA, and at the end reads O from TMEM, divides by the sum,
 //               applies the sigmoid output gate and stores.
+// For D = 128 the softmax writes P back into tensor memory over the first 32
+// columns of its own S buffer (bf16 pairs), and the P.V MMA reads A from
+// there.  Without the two shared-memory P buffers the CTA takes 97 KB, so two
+// CTAs share an SM (256 TMEM columns each) and one CTA's softmax overlaps the
+// other's MMAs.  The next QK^T into that S buffer is issued after the P.V
+// that reads it, and one thread's tcgen05.mma instructions run in order.
 // The running max is only moved (and O rescaled through TMEM) when it grows
 // by more than 2^8 (log2 units): between moves P is computed against a stale
 // max, which the final division cancels exactly.
@@ -49,12 +56,13 @@ struct AttnTcArgs {
 template <int D>
 struct AttnTcShape {
   static constexpr int BQ = 128, BK = 64, ATOMS = D / 64;
+  static constexpr bool P_TMEM = D == 128;             // P over its S buffer in tensor memory
   static constexpr uint32_t Q_BYTES = BQ * D * 2;      // ATOMS x [128 rows x 128 B]
   static constexpr uint32_t KV_BYTES = BK * D * 2;     // ATOMS x [64 rows x 128 B]
   static constexpr uint32_t P_BYTES = BQ * BK * 2;     // [128 rows x 128 B]
   static constexpr uint32_t TMEM_COLS = D + 2 * BK <= 256 ? 256 : 512;
   static constexpr uint32_t S_COL = 0, O_COL = 2 * BK;  // S buffers at 0 and 64, O at 128
-  static constexpr size_t SMEM = 1024 + Q_BYTES + 4 * KV_BYTES + 2 * P_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + Q_BYTES + 4 * KV_BYTES + (P_TMEM ? 0 : 2 * P_BYTES) + 256;
 };
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -85,7 +93,7 @@ __device__ __forceinline__ uint64_t smem_desc_mn128(uint32_t saddr, uint32_t lbo
 }
 
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_out, AttnTcArgs a) {
   using Sh = AttnTcShape<D>;
   constexpr int BQ = Sh::BQ, BK = Sh::BK, ATOMS = Sh::ATOMS;
@@ -98,8 +106,8 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + Sh::Q_BYTES;        // 2 stages
   uint8_t* sV = sK + 2 * Sh::KV_BYTES;   // 2 stages
-  uint8_t* sP = sV + 2 * Sh::KV_BYTES;   // 2 buffers
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Sh::P_BYTES);
+  uint8_t* sP = sV + 2 * Sh::KV_BYTES;   // 2 buffers (none when P lives in tensor memory)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + (Sh::P_TMEM ? 0 : 2 * Sh::P_BYTES));
   uint64_t* qfull = bars;
   uint64_t* kfull = bars + 1;
   uint64_t* kempty = bars + 3;
@@ -218,12 +226,19 @@ __global__ void __launch_bounds__(192, 1)
             !mbar_wait(&vfull[s], ph, a.status, kTimeoutAttention))
           return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + s * Sh::P_BYTES);
         const uint32_t v_addr = smem_u32(sV + s * Sh::KV_BYTES);
+        if constexpr (Sh::P_TMEM) {
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          umma_bf16(tmem + Sh::O_COL, smem_desc_k128(p_addr + kk * 32), smem_desc_mn128(v_addr + kk * 16 * 128, BK * 128),
-                    IDESC_PV, (u > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk)  // 16 keys of P = 8 TMEM columns
+            umma_bf16_ts(tmem + Sh::O_COL, tmem + Sh::S_COL + s * BK + kk * 8,
+                         smem_desc_mn128(v_addr + kk * 16 * 128, BK * 128), IDESC_PV, (u > 0 || kk > 0) ? 1u : 0u);
+        } else {
+          const uint32_t p_addr = smem_u32(sP + s * Sh::P_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(tmem + Sh::O_COL, smem_desc_k128(p_addr + kk * 32),
+                      smem_desc_mn128(v_addr + kk * 16 * 128, BK * 128), IDESC_PV, (u > 0 || kk > 0) ? 1u : 0u);
+        }
         umma_commit(&vempty[s]);
         umma_commit(&pempty[s]);
         umma_commit(ofull);
@@ -393,6 +408,32 @@ __global__ void __launch_bounds__(192, 1)
       if (!__all_sync(0xffffffffu, pe)) {
         ok = false;
         break;
+      }
+      if constexpr (Sh::P_TMEM) {
+        uint32_t pw[32];
+        if (m < 0.5f * kMaskFill * scale_log2) {  // every key so far masked: P = 1 (see below)
+          const uint32_t one = pack_bf16x2(1.f, 1.f);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) pw[e] = one;
+          l += 64.f;
+        } else {
+          const float neg_m = -m;
+          float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * e]), scale_log2, neg_m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * e + 1]), scale_log2, neg_m));
+            ps[(2 * e) & 7] += p0;
+            ps[(2 * e + 1) & 7] += p1;
+            pw[e] = pack_bf16x2(p0, p1);
+          }
+          l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        }
+        tmem_st32(tmem + t_lane + Sh::S_COL + s * BK, pw);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&pfull[s]);
+        continue;
       }
       uint8_t* prow = sP + s * Sh::P_BYTES + r * 128;
       if (m < 0.5f * kMaskFill * scale_log2) {

@@ -239,13 +239,15 @@ def test_qk_norm_rope(dtype, d, prf):
     np.testing.assert_array_equal(got[..., hq * 2 * d + hkv * d :], qkv[..., hq * 2 * d + hkv * d :])  # v untouched
 
 
-def attention_case(dtype, d, s, softcap=0.0, window=0, lengths=None, seed=0):
+def attention_case(dtype, d, s, softcap=0.0, window=0, lengths=None, seed=0, qscale=1.0):
     import torch
 
     rng = np.random.default_rng(seed + d + s)
     b, hq, hkv = 2, 4, 2
     n = hq * 2 * d + 2 * hkv * d
-    qkv = O.cast(rng.standard_normal((b, s, n)).astype(F32), dtype)
+    qkv = rng.standard_normal((b, s, n)).astype(F32)
+    qkv[..., : hq * 2 * d] *= F32(qscale)  # large scores: the running max moves and O is rescaled
+    qkv = O.cast(qkv, dtype)
     lengths = lengths or [s, max(1, s - 37)]
     mask = np.arange(s)[None] < np.array(lengths)[:, None]
     out = torch.zeros((b * s, hq * d), dtype=torch.bfloat16 if dtype == "bf16" else torch.float32, device="cuda")
@@ -271,22 +273,32 @@ def test_attention_bf16_flash(d, s):
     assert np.abs(got - expected).mean() < 2e-3
 
 
+@pytest.mark.parametrize("d", [128, 256])
+def test_attention_bf16_long_rows_with_rescales(d):
+    """Many 64-key tiles per query tile, scores large enough that the running
+    max moves by more than the lazy-rescale margin (head_dim 128 keeps P in
+    tensor memory; 256 in shared memory)."""
+    got, expected = attention_case("bf16", d, 1024, lengths=[1024, 700], qscale=6.0, seed=3)
+    np.testing.assert_allclose(got, expected, rtol=2e-2, atol=2e-2)
+    assert np.abs(got - expected).mean() < 2e-3
+
+
 @pytest.mark.parametrize("d", [8, 64, 256])
 def test_attention_fp32_exact(d):
     got, expected = attention_case("fp32", d, 130)
     np.testing.assert_allclose(got, expected, rtol=1e-4, atol=1e-5)
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
-def test_attention_beyond_reference_flags(dtype):
-    got, expected = attention_case(dtype, 64, 200, softcap=5.0, window=48)
+@pytest.mark.parametrize("dtype,d", [("bf16", 64), ("bf16", 128), ("fp32", 64)])
+def test_attention_beyond_reference_flags(dtype, d):
+    got, expected = attention_case(dtype, d, 200, softcap=5.0, window=48)
     tol = dict(rtol=2e-2, atol=2e-2) if dtype == "bf16" else dict(rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(got, expected, **tol)
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "fp32"])
-def test_attention_length_one_row(dtype):
+@pytest.mark.parametrize("dtype,d", [("bf16", 64), ("bf16", 128), ("fp32", 64)])
+def test_attention_length_one_row(dtype, d):
     """A state whose only valid key is key 0: every later query attends to it alone."""
-    got, expected = attention_case(dtype, 64, 66, lengths=[1, 66])
+    got, expected = attention_case(dtype, d, 66, lengths=[1, 66])
     tol = dict(rtol=2e-2, atol=2e-2) if dtype == "bf16" else dict(rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(got, expected, **tol)
