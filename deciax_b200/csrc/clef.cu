@@ -230,11 +230,13 @@ static void launch_tc_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const G
   CUDA_CHECK(cudaGetLastError());
 }
 
-// Launch the CTA-pair GEMM: clusters of 2, as many as can be resident at once.
-template <int EPI>
-static void launch_tc_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, cudaStream_t st) {
+// Launch the CTA-pair GEMM: clusters of 2, as many as can be resident at once
+// (TPR: with the fused tensor-parallel reduction and its four extra warps).
+template <int EPI, bool TPR = false>
+static void launch_tc_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, cudaStream_t st,
+                                const TpFuse& tpf = TpFuse{}) {
   using S = Gemm2Shape;
-  auto kern = gemm_bf16_sm100_pair<EPI>;
+  auto kern = gemm_bf16_sm100_pair<EPI, TPR>;
   static std::mutex mu;
   static std::map<int, int> max_clusters;
   const int dev = current_device();
@@ -244,7 +246,7 @@ static void launch_tc_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, co
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(TPR ? 192 + 32 * kTpReduceWarps : 192);
   cfg.dynamicSmemBytes = S::SMEM;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -265,7 +267,7 @@ static void launch_tc_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, co
   }
   const int tiles = ((args.M + S::BM - 1) / S::BM) * ((args.N + S::BN - 1) / S::BN);
   cfg.gridDim = dim3(2 * std::min(tiles, clusters));
-  CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+  CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, args, tpf));
 }
 
 // bf16 GEMM on tcgen05.  A [M, K] (lda), B [N, K] (ldb).  Large problems run
@@ -626,6 +628,7 @@ struct Workspace {
   int b = 0, s = 0, lx = 0, o = 0, q = 0;
   DBuf ints, bytes;  // staged batch arrays (device)
   DBuf x, h, qkv, attn, gu, act, partial, gproj;
+  DBuf tp_flags;  // TP: tile flags of the fused GEMM + reduction (peers write them)
   DBuf memory, mnorm, kv;
   DBuf gv, questions, contexts, lexical;
   DBuf small;  // head buffers of size b*max(o,q)*max(W,FF,4W)
@@ -684,7 +687,9 @@ struct Model {
   // and residual stream, refreshed whenever the local buffers move.
   void* ipc_part_src = nullptr;
   void* ipc_x_src = nullptr;
-  std::vector<void*> peer_part, peer_x;
+  void* ipc_flags_src = nullptr;
+  std::vector<void*> peer_part, peer_x, peer_flags;
+  unsigned tp_epoch = 0;  // launches of the fused GEMM + reduction so far (the same on every rank)
   DBuf ipc_scratch, barrier_buf;
   bool p2p = false;  // peer pointers valid: TP reduction through tp_reduce_residual_kernel
 
@@ -693,9 +698,11 @@ struct Model {
       if (k == rank) continue;
       if (peer_part[k]) cudaIpcCloseMemHandle(peer_part[k]);
       if (peer_x[k]) cudaIpcCloseMemHandle(peer_x[k]);
+      if (k < static_cast<int>(peer_flags.size()) && peer_flags[k]) cudaIpcCloseMemHandle(peer_flags[k]);
     }
     peer_part.assign(tp, nullptr);
     peer_x.assign(tp, nullptr);
+    peer_flags.assign(tp, nullptr);
     p2p = false;
   }
 
@@ -785,9 +792,10 @@ struct Model {
   // Collective over the TP group: all ranks call it with the same buffer sizes.
   void exchange_ipc() {
     close_peers();
-    cudaIpcMemHandle_t h[2];
+    cudaIpcMemHandle_t h[3];
     CUDA_CHECK(cudaIpcGetMemHandle(&h[0], ws.partial.p));
     CUDA_CHECK(cudaIpcGetMemHandle(&h[1], ws.x.p));
+    CUDA_CHECK(cudaIpcGetMemHandle(&h[2], ws.tp_flags.p));
     const size_t hb = sizeof(h);
     ipc_scratch.ensure(static_cast<size_t>(tp) * hb);
     uint8_t* d = ipc_scratch.as<uint8_t>();
@@ -800,15 +808,18 @@ struct Model {
       if (k == rank) {
         peer_part[k] = ws.partial.p;
         peer_x[k] = ws.x.p;
+        peer_flags[k] = ws.tp_flags.p;
         continue;
       }
-      cudaIpcMemHandle_t hk[2];
+      cudaIpcMemHandle_t hk[3];
       std::memcpy(hk, all.data() + k * hb, hb);
       CUDA_CHECK(cudaIpcOpenMemHandle(&peer_part[k], hk[0], cudaIpcMemLazyEnablePeerAccess));
       CUDA_CHECK(cudaIpcOpenMemHandle(&peer_x[k], hk[1], cudaIpcMemLazyEnablePeerAccess));
+      CUDA_CHECK(cudaIpcOpenMemHandle(&peer_flags[k], hk[2], cudaIpcMemLazyEnablePeerAccess));
     }
     ipc_part_src = ws.partial.p;
     ipc_x_src = ws.x.p;
+    ipc_flags_src = ws.tp_flags.p;
     p2p = true;
   }
 
@@ -1294,7 +1305,16 @@ struct Model {
     if (any_linear) w.gproj.ensure(act_bytes(T * Ng_pad));
     if (dtype == CLEF_DTYPE_F32) w.gu.ensure(act_bytes(T * 2 * Fp));
     w.act.ensure(act_bytes(T * Fp));
-    if (tp > 1) w.partial.ensure(T * D * 4);
+    if (tp > 1) {
+      w.partial.ensure(T * D * 4);
+      // [tiles of 256 x 256][2 CTAs][4 warps][tp] flags of gemm_bf16_sm100_pair<kEpiF32, true>
+      const size_t fb = ((T + 255) / 256) * ((static_cast<size_t>(D) + 255) / 256) * 8 * tp * 4;
+      if (fb > w.tp_flags.bytes) {
+        w.tp_flags.alloc(fb);
+        // on the stream, before the handle exchange that lets peers write here
+        CUDA_CHECK(cudaMemsetAsync(w.tp_flags.p, 0, fb, stream));
+      }
+    }
     w.memory.ensure(act_bytes(T * W));
     w.mnorm.ensure(act_bytes(T * W));
     w.kv.ensure(act_bytes(T * 2 * W));
@@ -1311,7 +1331,9 @@ struct Model {
     w.lx = std::max(w.lx, lx);
     w.o = std::max(w.o, o);
     w.q = std::max(w.q, q);
-    if (tp > 1 && tp <= kTpMaxRanks && (w.partial.p != ipc_part_src || w.x.p != ipc_x_src)) exchange_ipc();
+    if (tp > 1 && tp <= kTpMaxRanks &&
+        (w.partial.p != ipc_part_src || w.x.p != ipc_x_src || w.tp_flags.p != ipc_flags_src))
+      exchange_ipc();
   }
 
   // -------------------------------------------------------------------------
@@ -1622,8 +1644,36 @@ struct Model {
       return;
     }
     float* part = ws.partial.as<float>();
-    if constexpr (sizeof(T) == 2)
+    if constexpr (sizeof(T) == 2) {
+      if (p2p && (tp == 2 || tp == 4 || tp == 8) && Tt >= 256 && D >= 256 && D % 8 == 0 && K % 8 == 0 &&
+          aligned16(in) && aligned16(w) &&
+          static_cast<void*>(x) == ws.x.p) {
+        // One kernel: the GEMM's FP32 partial tiles, flagged to their owners,
+        // reduced by the owners while later tiles' MMAs run; after the barrier
+        // every rank's x is complete.
+        GemmArgs args{Tt, D, K, part, D, nullptr, nullptr, 0, Lc.status};
+        TpFuse f{};
+        for (int k = 0; k < tp; ++k) {
+          f.parts[k] = static_cast<const float*>(peer_part[k]);
+          f.xs[k] = static_cast<bf16*>(peer_x[k]);
+          f.flags[k] = static_cast<unsigned*>(peer_flags[k]);
+        }
+        f.tp = tp;
+        f.rank = rank;
+        f.ldx = D;
+        f.epoch = ++tp_epoch;
+        const CUtensorMap ta = tmap_bf16(in, Tt, K, K, 128);
+        const CUtensorMap tb = tmap_bf16(w, D, K, K, 128);
+        launch_tc_gemm_pair<kEpiF32, true>(ta, tb, args, Lc.stream, f);
+        Lc.tick();
+        const int saved = Lc.cat;
+        tp_barrier(Lc);
+        Lc.mark(kCatAllReduce);
+        Lc.cat = saved;
+        return;
+      }
       gemm_bf16(Lc, kEpiF32, in, K, w, K, Tt, D, K, part, D, nullptr, nullptr, 0);
+    }
     else
       gemm_simt<T>(Lc, kSimtF32, in, K, w, K, Tt, D, K, part, D, nullptr, nullptr, 0);
     if (p2p) {

@@ -16,10 +16,24 @@
 // lives in the leader and gets one arrive per epilogue warp of both CTAs.
 // Epilogues are the one-CTA kernel's (gemm_sm100.cuh), per CTA on its 128
 // rows x 256 columns.  All waits are bounded.
+//
+// TPR (tensor parallelism): the o-proj / down-proj GEMM and the cross-rank
+// reduction after it run as one kernel, so the NVLink transfer overlaps the
+// MMAs of later tiles.  Every rank computes the same tiles in the same order
+// (its FP32 partial, the kEpiF32 epilogue); each epilogue warp, once its 32
+// rows of a tile are stored, publishes a flag in the memory of the tile's
+// owner (tp_tile_owner).  Six more warps per CTA (warps 6..11) reduce the
+// tiles this rank owns: they wait for the four epilogue warps' flags from
+// every rank, sum the tp partial rows in rank order (peer loads), add the
+// residual and write x = T(x + T(sum)) into every rank's x (peer stores) -- the semantics
+// of the unfused path in tp.cuh (qwen3_5/pallas.py:66-69,121).  Flags carry a
+// per-launch epoch, so they are never reset.  Plain peer loads and stores
+// only; no multicast.
 #pragma once
 
 #include "common.cuh"
 #include "gemm_sm100.cuh"
+#include "tp.cuh"
 
 namespace clef {
 
@@ -86,10 +100,106 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
       : "memory");
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(192, 1)
+// Peers of the fused TP reduction (TPR): index k = rank k's buffer.
+struct TpFuse {
+  const float* parts[kTpMaxRanks];  // FP32 partial [M, ldo] = this GEMM's output on rank k
+  __nv_bfloat16* xs[kTpMaxRanks];   // residual stream x [M, ldx]
+  unsigned* flags[kTpMaxRanks];     // tile flags [tiles][2 CTAs][4 warps][tp]
+  int tp, rank, ldx;
+  unsigned epoch;                   // this launch's flag value (every rank counts launches alike)
+};
+
+constexpr int kTimeoutTpFlag = 0x106;
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Owner of a tile: alternates along each cluster's tiles and across the
+// clusters of a wave, so every SM reduces 1/tp of its tiles and every rank
+// pulls at every moment.
+__device__ __forceinline__ int tp_tile_owner(int tile, int num_clusters, int tp) {
+  return (tile / num_clusters + tile % num_clusters) % tp;
+}
+
+// tpf.flags[k] for a run-time k, without a run-time index into the kernel
+// parameters (which would copy them to local memory).
+__device__ __forceinline__ unsigned* tp_flag_array(const TpFuse& f, int k) {
+  unsigned* r = f.flags[0];
+#pragma unroll
+  for (int j = 1; j < kTpMaxRanks; ++j)
+    if (j == k) r = f.flags[j];
+  return r;
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The reduce warps' share of an owned tile: the CTA's rows [row0, row0 +
+// nrows) x float4 columns [0, ncols4) from col0 (at most 128 x 64).  Item i is
+// row i / 64, float4 column i % 64; warp w, lane l takes items w*32 + l +
+// kTpReduceWarps*32*j, so each warp's loads are coalesced 512-byte runs.  R
+// items per lane are in flight at once (R x TP peer loads of 16 bytes): the
+// NVLink latency needs that much memory parallelism.
+constexpr int kTpReduceWarps = 6;
+
+template <int TP>
+__device__ __forceinline__ void tp_reduce_rows(const TpFuse& f, const __nv_bfloat16* own_x, int ldo, int row0,
+                                               int nrows, int col0, int ncols4, int item0) {
+  constexpr int R = 8 / TP;
+  constexpr int STRIDE = kTpReduceWarps * 32;
+  const float* parts[TP];
+  __nv_bfloat16* xs[TP];
+#pragma unroll
+  for (int k = 0; k < TP; ++k) {
+    parts[k] = f.parts[k];
+    xs[k] = f.xs[k];
+  }
+#pragma unroll 1
+  for (int base = item0; base < 128 * 64; base += STRIDE * R) {
+    float4 p[R][TP];
+    uint2 rv[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int i = base + STRIDE * j;
+      const int r = i >> 6, c = (i & 63) * 4;
+      if (i < 128 * 64 && r < nrows && (i & 63) < ncols4) {
+        const size_t po = static_cast<size_t>(row0 + r) * ldo + col0 + c;
+#pragma unroll
+        for (int k = 0; k < TP; ++k) p[j][k] = *reinterpret_cast<const float4*>(parts[k] + po);
+        rv[j] = *reinterpret_cast<const uint2*>(own_x + static_cast<size_t>(row0 + r) * f.ldx + col0 + c);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int i = base + STRIDE * j;
+      const int r = i >> 6, c = (i & 63) * 4;
+      if (!(i < 128 * 64 && r < nrows && (i & 63) < ncols4)) continue;
+      const size_t xo = static_cast<size_t>(row0 + r) * f.ldx + col0 + c;
+      float4 sum = p[j][0];
+#pragma unroll
+      for (int k = 1; k < TP; ++k) {  // rank order: the same bits on every rank
+        sum.x += p[j][k].x;
+        sum.y += p[j][k].y;
+        sum.z += p[j][k].z;
+        sum.w += p[j][k].w;
+      }
+      const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rv[j].x));
+      const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rv[j].y));
+      const uint2 o = make_uint2(pack_bf16x2(r0.x + round_to<__nv_bfloat16>(sum.x), r0.y + round_to<__nv_bfloat16>(sum.y)),
+                                 pack_bf16x2(r1.x + round_to<__nv_bfloat16>(sum.z), r1.y + round_to<__nv_bfloat16>(sum.w)));
+#pragma unroll
+      for (int k = 0; k < TP; ++k) *reinterpret_cast<uint2*>(xs[k] + xo) = o;
+    }
+  }
+}
+
+template <int EPI, bool TPR = false>
+__global__ void __launch_bounds__(TPR ? 192 + 32 * kTpReduceWarps : 192, 1)
     gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                         GemmArgs args) {
+                         GemmArgs args, const __grid_constant__ TpFuse tpf) {
+  static_assert(!TPR || EPI == kEpiF32, "the fused TP reduction follows the FP32-partial epilogue");
   using S = Gemm2Shape;
   constexpr int BK = S::BK, STAGES = S::STAGES;
   constexpr uint32_t IDESC = idesc_bf16_f32(256, 256);
@@ -207,7 +317,7 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit_pair(drain);
       mbar_wait(drain, 0, args.status, kTimeoutDrain);
     }
-  } else {
+  } else if (warp < 6) {
     const int q = warp & 3;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
     int local = 0;
@@ -229,7 +339,57 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + acc * 8);
+      if constexpr (TPR) {
+        // this warp's 32 partial rows are stored: tell the tile's owner
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) {
+          const size_t slot = ((static_cast<size_t>(tile) * 2 + rank) * 4 + q) * tpf.tp + tpf.rank;
+          st_release_sys(tp_flag_array(tpf, tp_tile_owner(tile, num_clusters, tpf.tp)) + slot, tpf.epoch);
+        }
+      }
     }
+  } else if constexpr (TPR) {
+    // ---- reduce warps: the tiles this rank owns, this CTA's 128 rows of each ----
+    const int tp = tpf.tp;
+    const __nv_bfloat16* own_x = tpf.xs[0];
+    for (int k = 1; k < kTpMaxRanks; ++k)  // tpf.xs[tpf.rank] without a run-time index into the parameters
+      if (k == tpf.rank) own_x = tpf.xs[k];
+    const int item0 = (warp - 6) * 32 + lane;
+    bool ok = true;
+    for (int tile = cluster; ok && tile < num_tiles; tile += num_clusters) {
+      if (tp_tile_owner(tile, num_clusters, tp) != tpf.rank) continue;
+      int m, n;
+      gemm_tile_coords(tile, num_m, num_n, m, n);
+      // every rank's four epilogue warps have stored their rows of this tile:
+      // flags [q][src] of this (tile, CTA), one per lane
+      const unsigned* f = tp_flag_array(tpf, tpf.rank) + (static_cast<size_t>(tile) * 2 + rank) * 4 * tp;
+      bool arrived = lane >= 4 * tp || ld_acquire_sys(f + lane) >= tpf.epoch;
+      const long long t0 = clock64();
+      while (!__all_sync(0xffffffffu, arrived)) {
+        if (!arrived) arrived = ld_acquire_sys(f + lane) >= tpf.epoch;
+        if (clock64() - t0 > 2 * kWaitCycles || *abort_flag) {
+          record_status(args.status, kTimeoutTpFlag);
+          arrived = true;
+          ok = false;
+        }
+        __nanosleep(64);
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const int row0 = m * S::BM + static_cast<int>(rank) * 128;
+      const int nrows = min(128, args.M - row0);
+      const int ncols4 = (min(args.N, (n + 1) * S::BN) - n * S::BN) / 4;
+      if (nrows > 0) {
+        switch (tp) {
+          case 2: tp_reduce_rows<2>(tpf, own_x, args.ldo, row0, nrows, n * S::BN, ncols4, item0); break;
+          case 4: tp_reduce_rows<4>(tpf, own_x, args.ldo, row0, nrows, n * S::BN, ncols4, item0); break;
+          case 8: tp_reduce_rows<8>(tpf, own_x, args.ldo, row0, nrows, n * S::BN, ncols4, item0); break;
+          default: record_status(args.status, kTimeoutTpFlag); break;  // the host launches only tp = 2, 4, 8
+        }
+      }
+    }
+    __threadfence_system();  // peer stores ordered before the barrier that follows the launch
   }
 
   tc_fence_before();

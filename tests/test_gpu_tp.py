@@ -126,6 +126,13 @@ def test_tp2_bf16_probabilities(kind):
     from gpu_helpers import probs_close
 
     results = _run_tp(2, "bf16", kind)
-    arrays, exp_logits, _ = _oracle("bf16", kind)
+    arrays, exp_logits, exp_hidden = _oracle("bf16", kind)
     err, flips = probs_close(results[0][0], exp_logits, arrays)
     assert err < 1e-2 and flips == 0, (err, flips)
+    # bf16 TP runs the fused GEMM + peer reduction: each owner writes its rows
+    # into every rank's residual stream, so both ranks hold the same bits
+    np.testing.assert_array_equal(results[0][1], results[1][1])
+    valid = arrays["mask"]
+    got, exp = results[0][1][valid], exp_hidden[valid]
+    scale = np.abs(exp).max()
+    assert np.abs(got - exp).max() < 3e-2 * scale and np.abs(got - exp).mean() < 2e-3 * scale
