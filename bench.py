@@ -576,13 +576,25 @@ def serving_records(lengths, vocab: int, seed: int):
     return records, questions
 
 
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id from the library (made on rank 0, then shared)."""
+    from deciax_b200 import _lib
+
+    buf = ctypes.create_string_buffer(_lib.NCCL_ID_BYTES)
+    _lib.check(_lib.load().clef_nccl_unique_id(buf))
+    return buf.raw
+
+
 def serving_arm(args) -> None:
     """BASELINE cfg5: decide_batch of 256 states with lognormal lengths (median
     600, sigma 0.8, clipped to [32, 16384], seed 5), 4 choice x 4 options
     each, through ClefEngine (length-grouped batches, host arrays in, answers
     out), plus the max_len case of 4 x 16384 tokens.  Under torchrun each rank
     (one GPU, a full replica) serves every N-th state: data parallel, max over
-    ranks.  Reports decisions/s and p50/p99 per-batch latency."""
+    ranks.  With --serving-tp the N ranks instead form one tensor-parallel
+    model and every rank runs every batch (the engine's batch plan depends only
+    on the records, so the ranks stay in step); rank 0's answers count.
+    Reports decisions/s and p50/p99 per-batch latency."""
     import torch
 
     from deciax_b200.engine import ClefEngine
@@ -599,12 +611,17 @@ def serving_arm(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
     c = CFG5
+    tp = world if args.serving_tp and world > 1 else 1
     rng = np.random.default_rng(c["seed"])
     lengths = np.clip(np.round(rng.lognormal(np.log(c["median"]), c["sigma"], c["states"])), c["min"], c["max"]).astype(int)
-    sweep, questions = serving_records(lengths[rank::world], CFG2["vocab_size"], seed=10 + rank)
     longs, _ = serving_records([c["max"]] * c["long"], CFG2["vocab_size"], seed=20)
-    longs = longs[rank::world]
-    model = build_model(local, max_seq_len=c["max"])
+    if tp > 1:
+        sweep, questions = serving_records(lengths, CFG2["vocab_size"], seed=10)
+        model = build_model(local, max_seq_len=c["max"], tp_rank=rank, tp_size=tp, nccl_id=share_from_rank0(nccl_unique_id))
+    else:
+        sweep, questions = serving_records(lengths[rank::world], CFG2["vocab_size"], seed=10 + rank)
+        longs = longs[rank::world]
+        model = build_model(local, max_seq_len=c["max"])
     engine = ClefEngine(model)
 
     def run(records, timings=None):
@@ -633,8 +650,9 @@ def serving_arm(args) -> None:
 
     sweep_s = agg(statistics.mean(sweep_t), "max")
     long_s = agg(statistics.mean(long_t), "max")
-    decisions = agg(float(len(sweep) * QUESTIONS), "sum")
-    tokens = agg(float(sum(len(r.ids) for r in sweep)), "sum")
+    count = "max" if tp > 1 else "sum"  # TP ranks serve the same states; DP ranks disjoint ones
+    decisions = agg(float(len(sweep) * QUESTIONS), count)
+    tokens = agg(float(sum(len(r.ids) for r in sweep)), count)
     p50, p99 = agg(pct([t for *_, t in timings], 50), "max"), agg(pct([t for *_, t in timings], 99), "max")
     lp50 = agg(pct([t for *_, t in long_timings], 50), "max")
     if dist:
@@ -646,7 +664,8 @@ def serving_arm(args) -> None:
             "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
             "data": "synthetic (random-init weights, uniform token ids, lognormal lengths)",
             "config": {"workload": "cfg5", "states": c["states"], "lengths": "lognormal(log 600, 0.8) clipped [32, 16384], seed 5",
-                       "total_tokens": int(lengths.sum()), "parallelism": f"dp{world}" if world > 1 else "single",
+                       "total_tokens": int(lengths.sum()),
+                       "parallelism": f"tp{tp}" if tp > 1 else (f"dp{world}" if world > 1 else "single"),
                        "batching": "ClefEngine length-grouped, max_batch_tokens 65536"},
             "prefill_tokens_per_s": tokens / sweep_s, "sweep_seconds": sweep_s,
             "batch_latency_ms": {"p50": p50, "p99": p99, "batches_per_rank": len(timings) // max(args.steps, 1)},
@@ -729,12 +748,11 @@ def mixed_records(states: int, length: int, vocab: int, seed: int):
 def cfg4_arm(args) -> None:
     """BASELINE cfg4: the clef-shaped 27B model (46 layers, hidden 4608, 32 q /
     16 kv heads of 128, MLP 36864, vocab 256000), BF16, tensor-parallel over
-    the N ranks of torchrun (heads and MLP columns sharded, FP32 all-reduce of
-    the o-proj and down-proj partials over NCCL), one batch of 16 states x
-    8192 tokens per step (64 fields, 448 options per state).  Strong scaling:
-    the work per step is fixed; value = the group's tokens/s."""
-    import ctypes as ct
-
+    the N ranks of torchrun (heads and MLP columns sharded; the o-proj and
+    down-proj partials summed in FP32 across ranks over NVLink peer memory
+    inside the projection kernel), one batch of 16 states x 8192 tokens per
+    step (64 fields, 448 options per state).  Strong scaling: the work per
+    step is fixed; value = the group's tokens/s."""
     import torch
 
     from deciax_b200 import _lib
@@ -752,12 +770,7 @@ def cfg4_arm(args) -> None:
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
-        def make_id() -> bytes:
-            buf = ct.create_string_buffer(_lib.NCCL_ID_BYTES)
-            _lib.check(_lib.load().clef_nccl_unique_id(buf))
-            return buf.raw
-
-        nccl_id = share_from_rank0(make_id)
+        nccl_id = share_from_rank0(nccl_unique_id)
     c = CFG4_BATCH
     model = build_model(local, max_seq_len=c["seq"], cfg=CFG4, tp_rank=rank, tp_size=world, nccl_id=nccl_id)
     arrays = collate(mixed_records(c["states"], c["seq"], CFG4["vocab_size"], seed=31), 0)
@@ -907,6 +920,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--serving-tp", action="store_true",
+                    help="cfg5 under torchrun: one tensor-parallel model over the N GPUs instead of N replicas")
     ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg4", "cfg5", "attention", "attention4", "gdn", "rmsnorm"), default="cfg2",
                     help="cfg2 = the full prefill+scoring step (default); cfg3 = the GEMM microbenchmark; "
                     "cfg5 = the serving sweep through ClefEngine; attention = cfg2's attention layer alone; "
