@@ -1645,9 +1645,14 @@ struct Model {
     }
     float* part = ws.partial.as<float>();
     if constexpr (sizeof(T) == 2) {
-      if (p2p && (tp == 2 || tp == 4 || tp == 8) && Tt >= 256 && D >= 256 && D % 8 == 0 && K % 8 == 0 &&
-          aligned16(in) && aligned16(w) &&
-          static_cast<void*>(x) == ws.x.p) {
+      // The fused kernel pays off while the GEMM is not much shorter than its
+      // reduction: GEMM time ~ K, NVLink bytes per rank ~ 4 (tp-1)/tp per
+      // output element, so K tp / (tp-1) >= 1536 (measured on cfg4: o-proj at
+      // TP=8, K = 512, runs faster unfused; down-proj at every tp and o-proj
+      // at TP=2 faster fused; o-proj at TP=4, K = 1024, the same either way).
+      const bool fuse = static_cast<long long>(K) * tp >= 1536LL * (tp - 1);
+      if (fuse && p2p && (tp == 2 || tp == 4 || tp == 8) && Tt >= 256 && D >= 256 && D % 8 == 0 && K % 8 == 0 &&
+          aligned16(in) && aligned16(w) && static_cast<void*>(x) == ws.x.p) {
         // One kernel: the GEMM's FP32 partial tiles, flagged to their owners,
         // reduced by the owners while later tiles' MMAs run; after the barrier
         // every rank's x is complete.

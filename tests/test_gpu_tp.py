@@ -24,11 +24,13 @@ def _config(kind: str):
     head = HeadConfig(heads=4, routing_layers=1, layers=1, width=64, ffn=128)
     if kind == "mixed":  # Gated DeltaNet layers shard by key/value heads (qwen3_5/pallas.py:84-90)
         return TextConfig(
-            hidden_size=512, intermediate_size=1024, num_attention_heads=4, num_key_value_heads=2, head_dim=256,
+            hidden_size=512, intermediate_size=3072, num_attention_heads=4, num_key_value_heads=2, head_dim=256,
             linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=64, linear_value_head_dim=64,
             linear_conv_kernel_dim=4, layer_types=("linear_attention", "full_attention"), rms_norm_eps=1e-6,
             rope_theta=10000.0, partial_rotary_factor=0.25, vocab_size=300), head
-    return TextConfig.full_attention(hidden_size=512, intermediate_size=1024, num_attention_heads=4, num_key_value_heads=2,
+    # intermediate 3072: at TP=2 the down-proj (K = 1536) runs the fused GEMM + peer reduction in
+    # bf16, the o-proj (K = 512) the unfused pull kernel
+    return TextConfig.full_attention(hidden_size=512, intermediate_size=3072, num_attention_heads=4, num_key_value_heads=2,
                                      head_dim=256, num_layers=2, vocab_size=300), head
 
 
