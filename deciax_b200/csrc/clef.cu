@@ -1985,9 +1985,12 @@ struct Model {
     CUDA_CHECK(cudaMemcpy(&s, status.p, sizeof(int), cudaMemcpyDeviceToHost));
     if (s != 0) {
       CUDA_CHECK(cudaMemset(status.p, 0, sizeof(int)));
-      char buf[96];
-      std::snprintf(buf, sizeof(buf), "device status 0x%x (%s)", s,
-                    s == kBadIndex ? "token id out of range" : "pipeline wait timed out");
+      const char* what = s == kBadIndex         ? "token id out of range"
+                         : s == kTimeoutTpFlag  ? "a tensor-parallel peer's tile did not arrive in time"
+                         : s == kBadTpRanks     ? "fused tensor-parallel reduction launched for an unsupported rank count"
+                                                : "pipeline wait timed out";
+      char buf[160];
+      std::snprintf(buf, sizeof(buf), "device status 0x%x (%s)", s, what);
       throw Error(CLEF_EDEVICE, buf);
     }
   }

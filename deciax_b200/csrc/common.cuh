@@ -27,7 +27,9 @@ enum StatusCode : int {
   kTimeoutEpilogue = 0x103,
   kTimeoutDrain = 0x104,
   kTimeoutAttention = 0x105,
+  kTimeoutTpFlag = 0x106,  // a tensor-parallel peer's tile flag did not arrive
   kBadIndex = 0x201,
+  kBadTpRanks = 0x202,     // fused TP reduction launched for an unsupported rank count
 };
 
 // ---------------------------------------------------------------------------

@@ -109,8 +109,6 @@ struct TpFuse {
   unsigned epoch;                   // this launch's flag value (every rank counts launches alike)
 };
 
-constexpr int kTimeoutTpFlag = 0x106;
-
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -385,7 +383,7 @@ __global__ void __launch_bounds__(TPR ? 192 + 32 * kTpReduceWarps : 192, 1)
           case 2: tp_reduce_rows<2>(tpf, own_x, args.ldo, row0, nrows, n * S::BN, ncols4, item0); break;
           case 4: tp_reduce_rows<4>(tpf, own_x, args.ldo, row0, nrows, n * S::BN, ncols4, item0); break;
           case 8: tp_reduce_rows<8>(tpf, own_x, args.ldo, row0, nrows, n * S::BN, ncols4, item0); break;
-          default: record_status(args.status, kTimeoutTpFlag); break;  // the host launches only tp = 2, 4, 8
+          default: record_status(args.status, kBadTpRanks); break;  // the host launches only tp = 2, 4, 8
         }
       }
     }
