@@ -11,7 +11,8 @@ other rows or the padding of its batch:
 * records are grouped by length into batches whose padded size
   (rows x padded length) stays within ``max_batch_tokens``, instead of fixed
   pairs in input order; a batch is padded only to its longest record rounded
-  up to 128 tokens (not to a power-of-two bucket) and has no padded rows;
+  up to 128 tokens (not to a power-of-two bucket) and has no padded rows; the
+  cut points minimise a cost model of the padded work (``plan_batches``);
 * batches go to every replica at once (data parallelism: one model per GPU,
   each with full weights, no collective), one host thread per replica.  The
   library releases the GIL for the whole forward, so replicas run
@@ -39,30 +40,57 @@ from deciax_b200.clef_input import ROW_BUCKETS, Record, SchemaPrompt, collate, d
 
 DEFAULT_BATCH_TOKENS = 65536
 SEQ_ALIGN = 128
+# Cost model of one forward, in token-equivalents of linear-layer work (the
+# cfg2 clef-flash shape on one B200, where a token of padded work costs
+# ~16 us): a fixed cost per batch (launches, head, host collate/decode), a
+# floor below which the GPU is not filled, and causal attention's growth with
+# the padded length (per token ~ seq / ATTN_TOKENS of the linear work).
+BATCH_COST_TOKENS = 256
+MIN_BATCH_TOKENS = 4096
+ATTN_TOKENS = 24000
+
+
+def batch_cost(rows: int, seq: int) -> float:
+    """Modelled cost of one batch of ``rows`` records padded to ``seq``."""
+    padded = rows * seq
+    return BATCH_COST_TOKENS + max(padded, MIN_BATCH_TOKENS) + padded * seq / ATTN_TOKENS
 
 
 def plan_batches(lengths: Sequence[int], max_batch_tokens: int = DEFAULT_BATCH_TOKENS, max_rows: int = ROW_BUCKETS[-1],
-                 seq_align: int = SEQ_ALIGN, fill: float = 0.75) -> list[tuple[list[int], int]]:
+                 seq_align: int = SEQ_ALIGN) -> list[tuple[list[int], int]]:
     """Group record indices into (indices, padded length) batches, longest first.
 
-    A batch's padded length is its longest record rounded up to ``seq_align``;
-    later (shorter) records join while the batch stays within
-    ``max_batch_tokens`` and ``max_rows`` and each is at least ``fill`` of the
-    longest, so padding stays bounded.  A record longer than the budget
-    runs alone.
+    Records sorted longest first are cut into contiguous runs (with sorted
+    lengths the padding-optimal groups are contiguous); a run's padded length
+    is its first record rounded up to ``seq_align``, it holds at most
+    ``max_rows`` records and ``max_batch_tokens`` padded tokens (a record
+    longer than the budget runs alone).  The cut points minimise the summed
+    ``batch_cost`` by dynamic programming over (run start, run length), so
+    padding is traded against the per-batch cost instead of bounded by a fixed
+    length ratio.  The plan depends only on ``lengths``, so tensor-parallel
+    ranks that plan the same records run the same batches.
     """
     order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
-    batches: list[tuple[list[int], int]] = []
-    pos = 0
-    while pos < len(order):
-        seq = -(-lengths[order[pos]] // seq_align) * seq_align
+    n = len(order)
+    best = [0.0] + [float("inf")] * n  # best[j]: cost of the first j records
+    cut = [0] * (n + 1)
+    for i in range(n):  # a run starting at sorted position i
+        if best[i] == float("inf"):
+            continue
+        seq = -(-lengths[order[i]] // seq_align) * seq_align
         cap = max(1, min(max_rows, max_batch_tokens // seq))
-        end = pos + 1
-        while end < len(order) and end - pos < cap and lengths[order[end]] >= fill * lengths[order[pos]]:
-            end += 1
-        batches.append((order[pos:end], seq))
-        pos = end
-    return batches
+        for rows in range(1, min(cap, n - i) + 1):
+            c = best[i] + batch_cost(rows, seq)
+            if c < best[i + rows]:
+                best[i + rows] = c
+                cut[i + rows] = i
+    batches: list[tuple[list[int], int]] = []
+    j = n
+    while j > 0:
+        i = cut[j]
+        batches.append((order[i:j], -(-lengths[order[i]] // seq_align) * seq_align))
+        j = i
+    return batches[::-1]
 
 
 class ClefEngine:

@@ -193,15 +193,59 @@ def states(n, seed=0):
     return [" ".join(rng.choice(words, size=int(rng.integers(1, 400)))) for _ in range(n)]
 
 
-def test_plan_batches_bounds_padding_and_budget():
+def test_plan_batches_respects_budget_and_rows():
     lengths = [int(x) for x in np.random.default_rng(3).integers(50, 9000, size=137)]
     batches = plan_batches(lengths, max_batch_tokens=32768)
     assert sorted(i for idx, _ in batches for i in idx) == list(range(137))
+    order = sorted(range(137), key=lambda i: (-lengths[i], i))
+    assert [i for idx, _ in batches for i in idx] == order  # contiguous runs of the length order
     for idx, seq in batches:
         assert seq % 128 == 0 and max(lengths[i] for i in idx) <= seq < max(lengths[i] for i in idx) + 128
         assert len(idx) * seq <= 32768 or len(idx) == 1
-        assert all(lengths[i] >= 0.75 * lengths[idx[0]] for i in idx[1:])
+        assert len(idx) <= 64
     assert plan_batches([16384], 1024) == [([0], 16384)]  # one over-budget record runs alone
+    assert plan_batches([16384] * 4) == [([0, 1, 2, 3], 16384)]  # the max_len case: one batch
+    assert plan_batches([]) == []
+
+
+def test_plan_batches_minimises_the_cost_model():
+    """The cut points are optimal for ``batch_cost``: no single greedy plan
+    (any fixed length ratio) and no brute-force split of a small case beats
+    them, and on the serving sweep's lognormal lengths the plan pads little."""
+    from itertools import combinations
+
+    from deciax_b200.engine import batch_cost
+
+    def cost(batches):
+        return sum(batch_cost(len(idx), seq) for idx, seq in batches)
+
+    def greedy(lengths, fill, budget=65536, rows=64):
+        order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
+        out, pos = [], 0
+        while pos < len(order):
+            seq = -(-lengths[order[pos]] // 128) * 128
+            cap = max(1, min(rows, budget // seq))
+            end = pos + 1
+            while end < len(order) and end - pos < cap and lengths[order[end]] >= fill * lengths[order[pos]]:
+                end += 1
+            out.append((order[pos:end], seq))
+            pos = end
+        return out
+
+    rng = np.random.default_rng(5)
+    lengths = [int(x) for x in np.clip(np.round(rng.lognormal(np.log(600), 0.8, 256)), 32, 16384)]
+    plan = plan_batches(lengths)
+    for fill in (0.0, 0.5, 0.75, 0.85, 0.9, 0.95, 1.0):
+        assert cost(plan) <= cost(greedy(lengths, fill)) + 1e-6, fill
+    padded = sum(len(idx) * seq for idx, seq in plan)
+    assert sum(lengths) / padded > 0.9
+    small = [int(x) for x in rng.integers(100, 3000, size=9)]
+    order = sorted(range(9), key=lambda i: (-small[i], i))
+    best = min(
+        cost([(order[a:b], -(-small[order[a]] // 128) * 128) for a, b in zip((0, *cuts), (*cuts, 9))])
+        for k in range(9) for cuts in combinations(range(1, 9), k)
+    )
+    assert abs(cost(plan_batches(small)) - best) < 1e-6
 
 
 def test_engine_matches_per_record_answers_in_input_order():
