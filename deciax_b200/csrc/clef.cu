@@ -17,6 +17,7 @@
 
 #include <cudaTypedefs.h>
 #include <nccl.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <chrono>
@@ -189,6 +190,16 @@ struct Timeline {
   ~Timeline() {
     for (auto e : pool) cudaEventDestroy(e);
   }
+};
+
+// NVTX range for profilers (Nsight Systems / Compute): forward, layer, mixer,
+// MLP and head spans on the host timeline, around the kernels they launch.
+// Without a profiler attached the push / pop are no-op calls.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
 };
 
 struct Launcher {
@@ -1546,6 +1557,7 @@ struct Model {
   template <typename T>
   void forward_impl(const DevBatch& bt, float* logits, cudaStream_t st) {
     REQUIRE(finalized, "clef_forward before clef_finalize");
+    NvtxRange forward_range("clef forward");
     Launcher Lc{st, status.as<int>(), 0, kCatOther, &timeline};
     Lc.mark(-1);  // timeline start marker
     const int B = bt.b, S = bt.s;
@@ -1571,10 +1583,18 @@ struct Model {
     // 2. decoder layers (text.py:94-102; TP: pallas.py:62-129)
     for (int li = 0; li < L; ++li) {
       Layer& l = layers[li];
-      if (layer_types[li] == CLEF_LAYER_LINEAR_ATTENTION)
-        gdn_mixer<T>(Lc, l, bt, x, hbuf, attn_out, Tt);
-      else
-        attention_mixer<T>(Lc, l, li, bt, x, hbuf, qkv, attn_out, Tt);
+      const bool linear = layer_types[li] == CLEF_LAYER_LINEAR_ATTENTION;
+      char name[48];
+      std::snprintf(name, sizeof(name), "layer %d %s", li, linear ? "linear_attention" : "full_attention");
+      NvtxRange layer_range(name);
+      {
+        NvtxRange mixer_range(linear ? "gated deltanet" : "attention");
+        if (linear)
+          gdn_mixer<T>(Lc, l, bt, x, hbuf, attn_out, Tt);
+        else
+          attention_mixer<T>(Lc, l, li, bt, x, hbuf, qkv, attn_out, Tt);
+      }
+      NvtxRange mlp_range("mlp");
       Lc.cat = kCatNorm;
       rmsnorm<T>(Lc, x, D, l.w_post.as<T>(), hbuf, D, Tt, D, eps);
       Lc.cat = kCatGemmGateUp;
@@ -1595,7 +1615,10 @@ struct Model {
     rmsnorm<T>(Lc, x, D, final_norm.as<T>(), hbuf, D, Tt, D, eps);
     // 4-5. lexical means and the joint head
     Lc.cat = kCatHead;
-    scoring<T>(Lc, bt, logits);
+    {
+      NvtxRange head_range("lexical means + joint head");
+      scoring<T>(Lc, bt, logits);
+    }
     last_launches = Lc.count;
   }
 
