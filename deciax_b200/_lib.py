@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libclef_b200.so"
 CLEF_OK, CLEF_EINVAL, CLEF_ECUDA, CLEF_ENCCL, CLEF_EDEVICE, CLEF_ESTATE = range(6)
 DTYPE_F32, DTYPE_BF16 = 0, 1
 LAYER_FULL, LAYER_LINEAR = 0, 1
+DEBUG_POISON = 1  # CLEF_DEBUG_POISON
 NCCL_ID_BYTES = 128
 
 EXPORTS = (
@@ -31,6 +32,7 @@ EXPORTS = (
     "clef_set_timing",
     "clef_timing_report",
     "clef_last_launch_count",
+    "clef_set_debug",
     "clef_destroy",
     "clef_last_error",
     "clef_op_gemm",
@@ -132,6 +134,7 @@ def load() -> ctypes.CDLL:
             "clef_upload": [vp, ctypes.c_char_p, vp, i32, ctypes.POINTER(ctypes.c_int64), i32],
             "clef_upload_device": [vp, ctypes.c_char_p, vp, i32, ctypes.POINTER(ctypes.c_int64), i32],
             "clef_set_timing": [vp, i32],
+            "clef_set_debug": [vp, i32],
             "clef_timing_report": [vp, i32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int)],
             "clef_finalize": [vp],
             "clef_forward": [vp, ctypes.POINTER(ClefBatchC), vp, vp],

@@ -664,6 +664,7 @@ struct Model {
   cudaStream_t stream = nullptr;
   ncclComm_t comm = nullptr;
   int tp_timeout_ms = 0;  // longest host wait for the other TP ranks, 0 = no limit
+  int debug_flags = 0;    // CLEF_DEBUG_*
   bool broken = false;    // a TP wait ran out: a collective may still wait on the stream
   DBuf status;  // int
   DBuf embedding, lm_head, final_norm, rope_cos, rope_sin;
@@ -1554,10 +1555,20 @@ struct Model {
     project_residual<T>(Lc, core, g_nv_l * g_dh, l.g_out.as<T>(), x, Tt);
   }
 
+  // CLEF_DEBUG_POISON: NaN bytes over every scratch buffer a forward writes
+  // before it reads (not the staged batch, the flags or the status word).
+  void poison_scratch(cudaStream_t st) {
+    Workspace& w = ws;
+    for (DBuf* b : {&w.x, &w.h, &w.qkv, &w.attn, &w.gu, &w.act, &w.partial, &w.gproj, &w.memory, &w.mnorm, &w.kv,
+                    &w.gv, &w.questions, &w.contexts, &w.lexical, &w.small, &w.f32small})
+      if (b->p) CUDA_CHECK(cudaMemsetAsync(b->p, 0xFF, b->bytes, st));
+  }
+
   template <typename T>
   void forward_impl(const DevBatch& bt, float* logits, cudaStream_t st) {
     REQUIRE(finalized, "clef_forward before clef_finalize");
     NvtxRange forward_range("clef forward");
+    if (debug_flags & CLEF_DEBUG_POISON) poison_scratch(st);
     Launcher Lc{st, status.as<int>(), 0, kCatOther, &timeline};
     Lc.mark(-1);  // timeline start marker
     const int B = bt.b, S = bt.s;
@@ -2164,6 +2175,15 @@ int clef_check_status(void* handle) {
     CUDA_CHECK(cudaSetDevice(m->device));
     CUDA_CHECK(cudaDeviceSynchronize());
     m->check_status();
+  });
+}
+
+int clef_set_debug(void* handle, int flags) {
+  Model* m = static_cast<Model*>(handle);
+  return guarded(m, [&] {
+    REQUIRE(m, "null handle");
+    REQUIRE((flags & ~CLEF_DEBUG_POISON) == 0, "unknown debug flag");
+    m->debug_flags = flags;
   });
 }
 

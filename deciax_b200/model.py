@@ -170,6 +170,11 @@ class ClefCudaModel:
     def set_timing(self, enable: bool) -> None:
         _lib.check(self._lib.clef_set_timing(self._handle, int(enable)), self._handle)
 
+    def set_debug(self, poison: bool = False) -> None:
+        """Debug switches: ``poison`` fills the forward's scratch buffers with
+        NaN bytes before every forward (reads of unwritten memory show up)."""
+        _lib.check(self._lib.clef_set_debug(self._handle, _lib.DEBUG_POISON if poison else 0), self._handle)
+
     def timing_report(self) -> dict[str, tuple[float, int]]:
         """{category: (device ms, launches)} since the last report (see include/clef_b200.h)."""
         n = len(self.TIMING_CATEGORIES)

@@ -177,6 +177,15 @@ int clef_timing_report(void* handle, int n, float* ms, int* launches);
 /* Number of kernels the last forward launched (for launch accounting). */
 int clef_last_launch_count(void* handle);
 
+/* Debug switches (bit flags, 0 = off).  CLEF_DEBUG_POISON: before every
+ * forward, fill the forward's scratch buffers (activations, projections,
+ * head buffers, FP32 partials) with 0xFF bytes -- NaN in bf16 and fp32 -- so
+ * that a kernel reading memory it has not written first shows up as NaN or
+ * changed logits.  A sanitizer substitute for testing; it costs one memset
+ * per buffer per forward.  The reference has no counterpart. */
+#define CLEF_DEBUG_POISON 1
+int clef_set_debug(void* handle, int flags);
+
 int clef_destroy(void* handle);
 
 /* Message of the last failure on this handle (or of the last global failure when NULL). */

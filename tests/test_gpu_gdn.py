@@ -177,6 +177,21 @@ def test_mixed_model_bf16_probabilities():
     assert err < 1e-2 and flips == 0, (err, flips)
 
 
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_mixed_model_poisoned_scratch_changes_nothing(dtype):
+    """Gated DeltaNet layers under CLEF_DEBUG_POISON: NaN-filled scratch
+    buffers (the packed projection's padding columns included) change no bit
+    of the logits or real hidden states."""
+    model, _ = build(dtype)
+    arrays = synthetic_batch(SPEC, MIXED.vocab_size, seed=8)
+    base_logits, base_hidden = model.forward_with_hidden(arrays)
+    model.set_debug(poison=True)
+    logits, hidden = model.forward_with_hidden(arrays)
+    np.testing.assert_array_equal(logits, base_logits)
+    valid = arrays["mask"]
+    np.testing.assert_array_equal(hidden[valid], base_hidden[valid])
+
+
 def test_mixed_model_padding_does_not_leak():
     model, _ = build("fp32")
     arrays = synthetic_batch(SPEC, MIXED.vocab_size, seed=7)

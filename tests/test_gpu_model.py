@@ -115,6 +115,27 @@ def test_padding_does_not_leak():
     np.testing.assert_allclose(again[:3], base[:3], rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("config,dtype", [(SMALL, "fp32"), (SMALL, "bf16"), (WIDE, "bf16")])
+def test_poisoned_scratch_changes_nothing(config, dtype):
+    """Sanitizer substitute: with every scratch buffer filled with NaN bytes
+    before the forward (CLEF_DEBUG_POISON), logits and real hidden states stay
+    bit-identical, so no kernel reads memory it has not written first (tile
+    padding, stale rows of an earlier larger batch, unwritten head buffers)."""
+    model, _ = build(config, SMALL_HEAD, dtype)
+    big = synthetic_batch(SPECS["ragged"], config.vocab_size, seed=13)
+    small = synthetic_batch(SPECS["full"], config.vocab_size, seed=14)
+    model.forward(big)  # the workspace is sized for the larger batch first
+    for arrays in (small, big):
+        base_logits, base_hidden = model.forward_with_hidden(arrays)
+        model.set_debug(poison=True)
+        logits, hidden = model.forward_with_hidden(arrays)
+        model.set_debug(poison=False)
+        np.testing.assert_array_equal(logits, base_logits)
+        valid = arrays["mask"]
+        np.testing.assert_array_equal(hidden[valid], base_hidden[valid])
+        assert np.isfinite(logits[arrays["option_mask"]]).all()
+
+
 def test_beyond_reference_flags_match_oracle():
     flags = KernelFlags(attn_softcap=20.0, layer_window=(64, 0), embed_scale=2.0)
     model, weights = build(SMALL, SMALL_HEAD, "fp32", flags=flags)
