@@ -7,7 +7,8 @@ Writes, next to this script:
 * ``clef_head.npz`` / ``clef_head.json`` -- the reference deciax repository's
   own joint-head fixture (``tests/fixtures/clef_head.npz``: Cloudflare's torch
   ``JointSchemaHead`` outputs, seed 131), copied byte for byte from
-  REFERENCE_ROOT (default ``/root/reference``).  The reference test
+  REFERENCE_ROOT (the first argument, else the REFERENCE_ROOT environment
+  variable).  The reference test
   ``tests/clef/test_head.py:11-29`` compares against it at atol 3e-6 / rtol 3e-5.
 * ``qwen35_backbone_mixed.npz`` -- Transformers ``Qwen3_5TextModel`` at the
   configuration of the reference test ``tests/test_qwen3_5.py:43-87`` (three
@@ -27,12 +28,21 @@ from __future__ import annotations
 import hashlib
 import json
 import shutil
+import os
 import sys
 from pathlib import Path
 
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+
+
+def reference_root() -> Path:
+    """The reference checkout: the first argument, else $REFERENCE_ROOT."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT")
+    if not root:
+        raise SystemExit(f"usage: python {Path(__file__).name} REFERENCE_ROOT (or set REFERENCE_ROOT)")
+    return Path(root)
 
 
 def copy_head_fixture(reference: Path) -> None:
@@ -86,7 +96,7 @@ DIMS = dict(
 
 
 if __name__ == "__main__":
-    reference = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    reference = reference_root()
     copy_head_fixture(reference)
     backbone_fixture(
         "qwen35_backbone_mixed",

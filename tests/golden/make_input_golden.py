@@ -4,8 +4,9 @@ validation, ``encode``, ``collate`` and ``decode``).
 
     python tests/golden/make_input_golden.py [REFERENCE_ROOT]
 
-Imports the reference module from REFERENCE_ROOT/src (default
-``/root/reference``).  The reference package's ``__init__`` pulls in JAX, which
+Imports the reference module from REFERENCE_ROOT/src (the reference deciax
+checkout: the first argument, else the REFERENCE_ROOT environment variable).
+The reference package's ``__init__`` pulls in JAX, which
 this machine lacks and which the input module never touches, so the script
 registers an empty ``deciax`` package pointing at the sources and a stub
 ``jax`` module (only used there for type annotations in ``models/base.py``).
@@ -21,6 +22,7 @@ JSON.
 from __future__ import annotations
 
 import json
+import os
 import sys
 import types
 from pathlib import Path
@@ -28,6 +30,14 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+
+
+def reference_root() -> Path:
+    """The reference checkout: the first argument, else $REFERENCE_ROOT."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT")
+    if not root:
+        raise SystemExit(f"usage: python {Path(__file__).name} REFERENCE_ROOT (or set REFERENCE_ROOT)")
+    return Path(root)
 
 
 def import_reference(reference: Path):
@@ -98,7 +108,7 @@ INVALID = [
 
 
 def main() -> None:
-    reference = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    reference = reference_root()
     I = import_reference(reference)
 
     corpus = [I.SYSTEM_PROMPT, "SCHEMA FIELDS FIELD ID TYPE INSTRUCTION ALLOWED OPTIONS OPTION END STATE JOINT DECISIONS"]
