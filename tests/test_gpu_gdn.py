@@ -92,6 +92,51 @@ def test_gdn_core_matches_oracle(case, dtype):
         assert np.abs(got - expected).mean() < 2e-3 * scale
 
 
+def test_gdn_core_aligned_keys_with_weak_decay_are_stable():
+    """tests/test_qwen3_5.py:90-102 of the reference through the CUDA core: every
+    token's q = k (constant projections through a unit width-1 conv), decay
+    g = -exp(A_log) softplus(a + dt_bias) ~ -1e-5 and beta = sigmoid(b) ~ 0.996,
+    130 tokens, head dim 128, BF16.  The chunk's triangular system is then
+    nearly singular; the output must stay finite and match the oracle."""
+    lib = _lib.load()
+    import torch
+
+    b, s, nh, nv, dh, width, dtype = 1, 130, 2, 2, 128, 1, "bf16"
+    nk, nvd = nh * dh, nv * dh
+    n = 2 * nk + 2 * nvd + 2 * nv
+    proj = np.ones((b, s, n), np.float32)
+    # v differs across channels (the same for every token), so the gated norm
+    # at the end does not flatten the recurrence's output into a constant
+    proj[..., 2 * nk: 2 * nk + nvd] = np.random.default_rng(9).standard_normal(nvd).astype(np.float32)
+    proj[..., 2 * nk + 2 * nvd: 2 * nk + 2 * nvd + nv] = np.log(np.e - 1)  # a: softplus(a + 0) = 1
+    proj[..., 2 * nk + 2 * nvd + nv:] = np.log(0.996 / 0.004)  # b: beta ~ 0.996
+    proj = O.cast(proj, dtype)
+    conv = O.cast(np.ones((2 * nk + nvd, width), np.float32), dtype)
+    A_log = O.cast(np.full(nv, np.log(1e-5), np.float32), dtype)
+    dt_bias = O.cast(np.zeros(nv, np.float32), dtype)
+    norm_w = O.cast(np.ones(dh, np.float32), dtype)
+    cols = np.cumsum([0, nk, nk, nvd, nvd, nv, nv])
+    names = ("q", "k", "v", "in_proj_z", "in_proj_a", "in_proj_b")
+    projs = {k: proj[..., cols[i]:cols[i + 1]] for i, k in enumerate(names)}
+    p = {"q.conv": conv[:nk], "k.conv": conv[nk:2 * nk], "v.conv": conv[2 * nk:], "A_log": A_log, "dt_bias": dt_bias,
+         "norm.weight": norm_w}
+    c = O.TextConfig(hidden_size=8, intermediate_size=8, num_attention_heads=1, num_key_value_heads=1, head_dim=8,
+                     linear_num_key_heads=nh, linear_num_value_heads=nv, linear_key_head_dim=dh, linear_value_head_dim=dh,
+                     linear_conv_kernel_dim=width)
+    expected = O.delta_net_core(p, projs, c, dtype)
+    ldp = -(-n // 16) * 16
+    padded = np.zeros((b * s, ldp), np.float32)
+    padded[:, :n] = proj.reshape(b * s, -1)
+    tp, tc, ta, tb, tw = (dev(x, dtype) for x in (padded, conv, A_log, dt_bias, norm_w))
+    out = torch.full((b * s, nv * dh), float("nan"), device="cuda", dtype=tp.dtype)
+    _lib.check(lib.clef_op_gdn_core(_lib.DTYPE_BF16, tp.data_ptr(), ldp, tc.data_ptr(), width, ta.data_ptr(),
+                                    tb.data_ptr(), tw.data_ptr(), out.data_ptr(), b, s, nh, nv, dh, ctypes.c_float(1e-6), None))
+    got = host(out).reshape(expected.shape)
+    assert np.isfinite(got).all() and np.isfinite(expected).all()
+    scale = float(np.abs(expected).max())
+    np.testing.assert_allclose(got, expected, rtol=2e-2, atol=1e-2 * scale)
+
+
 def test_gdn_core_rejects_unsupported_head_dim():
     lib = _lib.load()
     import torch
