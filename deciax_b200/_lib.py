@@ -28,6 +28,7 @@ EXPORTS = (
     "clef_forward_head",
     "clef_forward_device",
     "clef_reserve",
+    "clef_workspace_allocations",
     "clef_check_status",
     "clef_set_timing",
     "clef_timing_report",
@@ -141,6 +142,7 @@ def load() -> ctypes.CDLL:
             "clef_forward_head": [vp, ctypes.POINTER(ClefBatchC), vp, vp],
             "clef_forward_device": [vp, ctypes.POINTER(ClefBatchC), vp, vp],
             "clef_reserve": [vp, i32, i32, i32, i32, i32],
+            "clef_workspace_allocations": [vp, ctypes.POINTER(ctypes.c_int64)],
             "clef_check_status": [vp],
             "clef_last_launch_count": [vp],
             "clef_destroy": [vp],

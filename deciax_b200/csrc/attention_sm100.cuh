@@ -298,6 +298,16 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       const int s = t & 1;
       const uint32_t ph = (t >> 1) & 1;
       const int k0 = (kb_lo + t) * BK;
+      const bool ready = mbar_wait(&sfull[s], ph, a.status, kTimeoutAttention);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, ready)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[64];  // the loads run while the key mask below is examined
+      tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+      tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       // Key validity for this tile (the same for every row): bit c = key k0 + c.
       uint32_t vbits[2] = {0xffffffffu, 0xffffffffu};
       if (k0 + BK > a.S) {
@@ -307,8 +317,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       }
       if (mrow) {
         if (a.mask_vec) {
-          // this tile's mask bytes were loaded during the previous tile; start
-          // the next tile's loads now so their latency overlaps this tile
+          // this tile's mask bytes were loaded at the end of the previous tile
           uint32_t all = 0x01010101u;
           uint4 w[4];
 #pragma unroll
@@ -316,7 +325,6 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
             w[v4] = mnext[v4];
             all &= w[v4].x & w[v4].y & w[v4].z & w[v4].w;
           }
-          load_mask(k0 + BK);
           if (all != 0x01010101u) {  // some key masked: build the bits (0/1 bytes)
             uint32_t bits[2] = {0u, 0u};
 #pragma unroll
@@ -334,16 +342,6 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
             if (k0 + c >= a.S || !mrow[k0 + c]) vbits[c >> 5] &= ~(1u << (c & 31));
         }
       }
-      const bool ready = mbar_wait(&sfull[s], ph, a.status, kTimeoutAttention);
-      __syncwarp();
-      if (!__all_sync(0xffffffffu, ready)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[64];
-      tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&sfree[s]);
@@ -433,6 +431,8 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&pfull[s]);
+        // next tile's mask bytes: loaded after the (release-ordered) arrive, so it does not wait for them
+        if (mrow && a.mask_vec) load_mask(k0 + BK);
         continue;
       }
       uint8_t* prow = sP + s * Sh::P_BYTES + r * 128;
@@ -465,6 +465,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&pfull[s]);
+      if (mrow && a.mask_vec) load_mask(k0 + BK);  // after the release-ordered arrive (see above)
     }
     if (!ok) *abort_flag = 1;
     // ---------------- epilogue ----------------

@@ -36,10 +36,12 @@
 #include "../../include/clef_b200.h"
 #include "attention.cuh"
 #include "attention_sm100.cuh"
+#include "attention_pair_sm100.cuh"
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm2_sm100.cuh"
 #include "gdn.cuh"
+#include "gdn_tc.cuh"
 #include "tp.cuh"
 #include "head.cuh"
 #include "simt.cuh"
@@ -79,6 +81,11 @@ static void set_global_error(const std::string& m) {
   std::lock_guard<std::mutex> lock(g_error_mutex);
   g_last_error = m;
 }
+
+// qk_norm_rope_kernel runs eight warps per block, each staging one head row
+// of head_dim floats in dynamic shared memory: 8 * head_dim * 4 bytes must
+// fit the default 48 KB.
+constexpr int kQkRopeMaxHeadDim = 48 * 1024 / (8 * 4);
 
 // ===========================================================================
 // host bf16 helpers
@@ -427,7 +434,26 @@ static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
     case 16: launch_gdn_dh<T, 16>(L, a); break;
     case 32: launch_gdn_dh<T, 32>(L, a); break;
     case 64: launch_gdn_dh<T, 64>(L, a); break;
-    case 128: launch_gdn_dh<T, 128>(L, a); break;
+    case 128:
+      if constexpr (sizeof(T) == 2) {
+        // bf16 activations at head dim 128: the tensor-core kernel (TF32 products, FP32 state and solve)
+        static std::mutex mu;
+        static std::set<int> done;
+        {
+          std::lock_guard<std::mutex> lock(mu);
+          if (!done.count(current_device())) {
+            CUDA_CHECK(cudaFuncSetAttribute(gdn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(GdnTcShape::SMEM)));
+            done.insert(current_device());
+          }
+        }
+        gdn_tc_kernel<<<dim3(a.nv, a.B), kGdnThreads, GdnTcShape::SMEM, L.stream>>>(a);
+        CUDA_CHECK(cudaGetLastError());
+        L.tick();
+      } else {
+        launch_gdn_dh<T, 128>(L, a);
+      }
+      break;
     default: throw Error(CLEF_EINVAL, "Gated DeltaNet head dim must be one of 8, 16, 32, 64, 128");
   }
 }
@@ -495,12 +521,35 @@ static void attention(Launcher& L, const AttnArgs<T>& a) {
         }
         kern<<<grid, 192, smem, L.stream>>>(map, out_map, t);
       };
-      if (a.hd == 64)
+      if (a.hd == 64) {
         launch(attn_tc_kernel<64>, AttnTcShape<64>::SMEM, 64);
-      else if (a.hd == 128)
+      } else if (a.hd == 128) {
         launch(attn_tc_kernel<128>, AttnTcShape<128>::SMEM, 128);
-      else
-        launch(attn_tc_kernel<256>, AttnTcShape<256>::SMEM, 256);
+      } else {
+        // head_dim 256: CTA pairs over 256 query rows and 128-key tiles
+        auto kern = attn_pair_kernel<256>;
+        constexpr size_t smem = AttnPairShape<256>::SMEM;
+        {
+          std::lock_guard<std::mutex> lock(mu_tc);
+          if (!done_tc.count({dev, -256})) {
+            CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+            done_tc.insert({dev, -256});
+          }
+        }
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * ((a.Lq + 255) / 256), a.H, a.B);
+        cfg.blockDim = dim3(AttnPairShape<256>::THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = L.stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, map, out_map, t));
+      }
       done = true;
     }
   }
@@ -674,6 +723,7 @@ struct Model {
   Workspace ws;
   Timeline timeline;
   int last_launches = 0;
+  int64_t ws_allocations = 0;  // workspace growths: device buffers, pinned staging, TP peer-handle exchanges
   bool src_on_device = false;  // clef_upload_device: the source pointer is device memory
 
   // Sum each category's device time over the recorded timeline, then reset it.
@@ -917,6 +967,7 @@ struct Model {
     // TP divisibility (the reference shards heads and MLP rows evenly, weights.py:60-67)
     REQUIRE(Hq % tp == 0 && Hkv % tp == 0 && F % tp == 0, "heads and intermediate size must divide by tp");
     REQUIRE(D % 8 == 0 && d % 8 == 0, "hidden size and head_dim must be multiples of 8");
+    REQUIRE(d <= kQkRopeMaxHeadDim, "head_dim must be at most 1536");
     Hq_l = Hq / tp;
     Hkv_l = Hkv / tp;
     F_l = F / tp;
@@ -1302,50 +1353,84 @@ struct Model {
     return static_cast<size_t>(b) * s + static_cast<size_t>(b) * q + static_cast<size_t>(b) * o;
   }
 
+  // Grow a workspace buffer to at least n bytes, counting the allocation.
+  void grow(DBuf& buf, size_t n) {
+    if (n <= buf.bytes) return;
+    buf.alloc(n);
+    ++ws_allocations;
+  }
+
+  // Pinned host staging of a host forward: the batch arrays and the logits.
+  void grow_pinned(size_t need) {
+    Workspace& w = ws;
+    if (w.pinned_bytes >= need) return;
+    if (w.host_pinned.p) {
+      cudaFreeHost(w.host_pinned.p);
+      w.host_pinned.p = nullptr;
+      w.pinned_bytes = 0;
+    }
+    CUDA_CHECK(cudaMallocHost(&w.host_pinned.p, need));
+    w.pinned_bytes = need;
+    ++ws_allocations;
+  }
+
+  size_t pinned_need(int b, int s, int lx, int o, int q) const {
+    return batch_int_count(b, s, lx, o, q) * 4 + batch_byte_count(b, s, o, q) + static_cast<size_t>(b) * o * 4 + 64;
+  }
+
   void reserve(int b, int s, int lx, int o, int q) {
     REQUIRE(b > 0 && s > 0 && lx > 0 && o > 0 && q > 0, "batch dimensions must be positive");
     REQUIRE(s <= cfg.max_seq_len, "sequence length exceeds max_seq_len");
     CUDA_CHECK(cudaSetDevice(device));
     Workspace& w = ws;
     const size_t T = static_cast<size_t>(b) * s;
-    w.ints.ensure(batch_int_count(b, s, lx, o, q) * 4 + 64);
-    w.bytes.ensure(batch_byte_count(b, s, o, q) + 64);
-    w.x.ensure(act_bytes(T * D));
-    w.h.ensure(act_bytes(T * D));
-    w.qkv.ensure(act_bytes(T * Nqkv));
-    w.attn.ensure(act_bytes(T * std::max(Hq_l * d, g_nv_l * g_dh)));
-    if (any_linear) w.gproj.ensure(act_bytes(T * Ng_pad));
-    if (dtype == CLEF_DTYPE_F32) w.gu.ensure(act_bytes(T * 2 * Fp));
-    w.act.ensure(act_bytes(T * Fp));
+    grow(w.ints, batch_int_count(b, s, lx, o, q) * 4 + 64);
+    grow(w.bytes, batch_byte_count(b, s, o, q) + 64);
+    grow(w.x, act_bytes(T * D));
+    grow(w.h, act_bytes(T * D));
+    grow(w.qkv, act_bytes(T * Nqkv));
+    grow(w.attn, act_bytes(T * std::max(Hq_l * d, g_nv_l * g_dh)));
+    if (any_linear) grow(w.gproj, act_bytes(T * Ng_pad));
+    if (dtype == CLEF_DTYPE_F32) grow(w.gu, act_bytes(T * 2 * Fp));
+    grow(w.act, act_bytes(T * Fp));
     if (tp > 1) {
-      w.partial.ensure(T * D * 4);
+      grow(w.partial, T * D * 4);
       // [tiles of 256 x 256][2 CTAs][4 warps][tp] flags of gemm_bf16_sm100_pair<kEpiF32, true>
       const size_t fb = ((T + 255) / 256) * ((static_cast<size_t>(D) + 255) / 256) * 8 * tp * 4;
       if (fb > w.tp_flags.bytes) {
-        w.tp_flags.alloc(fb);
+        grow(w.tp_flags, fb);
         // on the stream, before the handle exchange that lets peers write here
         CUDA_CHECK(cudaMemsetAsync(w.tp_flags.p, 0, fb, stream));
       }
     }
-    w.memory.ensure(act_bytes(T * W));
-    w.mnorm.ensure(act_bytes(T * W));
-    w.kv.ensure(act_bytes(T * 2 * W));
-    w.gv.ensure(act_bytes(static_cast<size_t>(b) * D));
-    w.questions.ensure(act_bytes(static_cast<size_t>(b) * q * D));
-    w.contexts.ensure(act_bytes(static_cast<size_t>(b) * o * D));
-    w.lexical.ensure(act_bytes(static_cast<size_t>(b) * o * D));
+    grow(w.memory, act_bytes(T * W));
+    grow(w.mnorm, act_bytes(T * W));
+    grow(w.kv, act_bytes(T * 2 * W));
+    grow(w.gv, act_bytes(static_cast<size_t>(b) * D));
+    grow(w.questions, act_bytes(static_cast<size_t>(b) * q * D));
+    grow(w.contexts, act_bytes(static_cast<size_t>(b) * o * D));
+    grow(w.lexical, act_bytes(static_cast<size_t>(b) * o * D));
     const size_t rows = static_cast<size_t>(b) * std::max(o, q);
     const size_t widest = std::max<size_t>({static_cast<size_t>(3 * W), static_cast<size_t>(FF), static_cast<size_t>(4 * W)});
-    w.small.ensure(act_bytes(rows * widest * 12 + static_cast<size_t>(b) * W * 2) + 16 * 64);
-    w.f32small.ensure(static_cast<size_t>(b) * o * 4 * 4 + 256);
+    grow(w.small, act_bytes(rows * widest * 12 + static_cast<size_t>(b) * W * 2) + 16 * 64);
+    grow(w.f32small, static_cast<size_t>(b) * o * 4 * 4 + 256);
     w.b = std::max(w.b, b);
     w.s = std::max(w.s, s);
     w.lx = std::max(w.lx, lx);
     w.o = std::max(w.o, o);
     w.q = std::max(w.q, q);
     if (tp > 1 && tp <= kTpMaxRanks &&
-        (w.partial.p != ipc_part_src || w.x.p != ipc_x_src || w.tp_flags.p != ipc_flags_src))
+        (w.partial.p != ipc_part_src || w.x.p != ipc_x_src || w.tp_flags.p != ipc_flags_src)) {
       exchange_ipc();
+      ++ws_allocations;
+    }
+  }
+
+  // clef_reserve: the device workspace and the pinned host staging of a host
+  // forward, for batches up to this shape.
+  void reserve_all(int b, int s, int lx, int o, int q) {
+    reserve(b, s, lx, o, q);
+    grow_pinned(pinned_need(b, s, lx, o, q));
   }
 
   // -------------------------------------------------------------------------
@@ -1549,6 +1634,7 @@ struct Model {
     a.nv = g_nv_l;
     a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(g_dh)));
     a.eps = cfg.rms_norm_eps;
+    a.status = Lc.status;
     Lc.cat = kCatGdn;
     launch_gdn<T>(Lc, a, g_dh);
     Lc.cat = kCatGemmO;
@@ -1924,16 +2010,7 @@ struct Model {
     reserve(b.b, b.s, b.lx, b.o, b.q);
     Workspace& w = ws;
     const size_t ni = batch_int_count(b.b, b.s, b.lx, b.o, b.q), nb = batch_byte_count(b.b, b.s, b.o, b.q);
-    const size_t nlog = static_cast<size_t>(b.b) * b.o;
-    const size_t need = ni * 4 + nb + nlog * 4 + 64;
-    if (w.pinned_bytes < need) {
-      if (w.host_pinned.p) {
-        cudaFreeHost(w.host_pinned.p);
-        w.host_pinned.p = nullptr;
-      }
-      CUDA_CHECK(cudaMallocHost(&w.host_pinned.p, need));
-      w.pinned_bytes = need;
-    }
+    grow_pinned(pinned_need(b.b, b.s, b.lx, b.o, b.q));
     uint8_t* hp = static_cast<uint8_t*>(w.host_pinned.p);
     int32_t* hi = reinterpret_cast<int32_t*>(hp);
     size_t o = 0;
@@ -2164,7 +2241,15 @@ int clef_reserve(void* handle, int b, int s, int lx, int o, int q) {
   Model* m = static_cast<Model*>(handle);
   return guarded(m, [&] {
     REQUIRE(m, "null handle");
-    m->reserve(b, s, lx, o, q);
+    m->reserve_all(b, s, lx, o, q);
+  });
+}
+
+int clef_workspace_allocations(void* handle, int64_t* count) {
+  Model* m = static_cast<Model*>(handle);
+  return guarded(m, [&] {
+    REQUIRE(m && count, "null handle or output");
+    *count = m->ws_allocations;
   });
 }
 
@@ -2287,6 +2372,8 @@ int clef_op_qk_norm_rope(int dtype, void* qkv, int b, int s, int hq, int hkv, in
     REQUIRE(qkv && q_norm && k_norm && b > 0 && s > 0 && hq > 0 && hkv > 0 && d > 0, "bad qk_norm_rope arguments");
     const int rot = static_cast<int>(d * partial_rotary_factor);
     REQUIRE(rot > 0 && rot % 2 == 0 && rot <= d, "invalid partial rotary dimension");
+    // eight warps, one d-float row each, in the default 48 KB of dynamic shared memory
+    REQUIRE(d <= clef::kQkRopeMaxHeadDim, "clef_op_qk_norm_rope supports head_dim <= 1536");
     std::vector<float> cs, sn;
     clef::rope_tables(s, rot, rope_theta, cs, sn);
     clef::DBuf dc, ds;
@@ -2436,14 +2523,28 @@ __global__ void noalloc_rope_table_kernel(float* __restrict__ cos_t, float* __re
   }
 }
 
-// Device address of g_noalloc_rope per device, looked up once per device with
-// that device current (the array's host-side name is not a device address).
-static float* noalloc_rope_scratch(int device) {
+// Device address of g_noalloc_rope on the current device.  The array's
+// host-side name is not a device address; cudaGetSymbolAddress, called with
+// the device current, gives it (the first call on a device loads the module
+// there).  Outside stream capture the address is looked up afresh on every
+// call, so a context that was reset and rebuilt (cudaDeviceReset) yields its
+// new address; while `st` is being captured the address last looked up on
+// this device is used, since loading a module is not allowed during capture.
+static float* noalloc_rope_scratch(int device, cudaStream_t st) {
   static std::mutex mu;
   static std::map<int, float*> addr;
   std::lock_guard<std::mutex> lock(mu);
-  auto it = addr.find(device);
-  if (it != addr.end()) return it->second;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) {
+    (void)cudaGetLastError();  // a legacy-stream query during another stream's capture: treat as capturing
+    cap = cudaStreamCaptureStatusActive;
+  }
+  if (cap != cudaStreamCaptureStatusNone) {
+    auto it = addr.find(device);
+    REQUIRE(it != addr.end(),
+            "clef_op_qk_norm_rope_noalloc: make one call on this device outside stream capture first");
+    return it->second;
+  }
   float* p = nullptr;
   CUDA_CHECK(cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_rope));
   addr[device] = p;
@@ -2462,15 +2563,16 @@ extern "C" int clef_op_qk_norm_rope_noalloc(int dtype, void* qkv, int b, int s, 
     REQUIRE(rot > 0 && rot % 2 == 0 && rot <= d, "invalid partial rotary dimension");
     const int half = rot / 2;
     REQUIRE(half <= 128, "clef_op_qk_norm_rope_noalloc supports rot/2 <= 128 (head_dim <= 256)");
+    REQUIRE(d <= clef::kQkRopeMaxHeadDim, "clef_op_qk_norm_rope_noalloc supports head_dim <= 1536");
     REQUIRE(static_cast<long long>(s) * half <= clef::kNoAllocRopeEntries,
             "clef_op_qk_norm_rope_noalloc: seq_len * rot/2 exceeds its fixed table of 1048576 entries");
     const int device = clef::current_device();
-    float* cos_t = clef::noalloc_rope_scratch(device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* cos_t = clef::noalloc_rope_scratch(device, st);
     float* sin_t = cos_t + clef::kNoAllocRopeEntries;
     clef::RopeFreqs f{};
     for (int i = 0; i < half; ++i)
       f.inv[i] = 1.0f / powf(rope_theta, static_cast<float>(2 * i) / static_cast<float>(rot));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long n = static_cast<long long>(s) * half;
     clef::noalloc_rope_table_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 1024)), 256, 0, st>>>(
         cos_t, sin_t, s, half, f);

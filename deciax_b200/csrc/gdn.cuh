@@ -39,6 +39,7 @@ struct GdnArgs {
   int B, S, nh, nv;
   float qscale;  // dk^-1/2 as a float32
   float eps;     // rms_norm_eps of the gated norm
+  int* status;   // device status word for a bounded wait that gives up (tensor-core kernel); may be null
 };
 
 constexpr int kGdnChunk = 64;

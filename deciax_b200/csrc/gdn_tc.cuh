@@ -1,0 +1,511 @@
+// Gated DeltaNet mixer core on the 5th-generation tensor cores (sm_100a),
+// BF16 activations, head dim 128: qwen3_5/text.py:48-67 with the chunked rule
+// of kernels/gdn/reference.py:40-92.
+//
+// One CTA per (state, value head) walks the sequence in 64-token chunks.  The
+// FP32 state S [dk, dv] stays in shared memory in the layout of a tcgen05
+// B operand.  Per chunk (c, c' tokens; i key dims; j value dims):
+//   L  conv + SiLU, L2 norms and gates as the CUDA-core kernel (gdn.cuh),
+//      written straight into operand layouts: A0 = [k; q] (128 rows), v.
+//   M0 D0 = A0 k^T (tcgen05, M = 128, N = 64, K = 128): rows 0-63 k k^T,
+//      rows 64-127 q k^T.
+//   P  rows 0-63 -> the strictly lower system A = -(k beta k^T) * decay;
+//      rows 64-127 -> M = (q k^T) * decay (c' <= c), written back into tensor
+//      memory as the A operand of M2; q -> q e^g in place; K~^T = (k e^{g_C - g})^T
+//      into tensor memory (the A operand of M3).
+//   T  exact forward substitution (I - A) X = [v beta | k beta e^g] on the
+//      CUDA cores, one right-hand column per thread, in place: U = X_v
+//      (reference.py:81 `value`), W = X_k (`cumulative_key`), so A0 = [W; q e^g].
+//   M1 D1 = A0 S (M = 128, N = 128, K = 128): rows 0-63 W S, rows 64-127 (q e^g) S.
+//   V  V_new = U - W S (reference.py:83), in place of U.
+//   M2 D1 += [. ; M] V_new (K = 64): rows 64-127 become the chunk's output
+//      (q e^g) S + (q k^T * decay) V_new (reference.py:85).
+//   M3 D2 = K~^T V_new (M = 128, N = 128, K = 64), then S = S e^{g_C} + D2
+//      (reference.py:86).
+//   O  gated RMSNorm x SiLU(z) of the output rows (text.py:61-67).
+// Products run as kind::tf32 (operands rounded to TF32, FP32 accumulation);
+// the solve, the gates and every elementwise step are FP32.  The FP32 parity
+// mode keeps the all-FP32 CUDA-core kernel.
+//
+// Layouts: every operand is rows of 32 fp32 (128 B) in atoms of `rows` rows
+// per 32 columns: a K-major operand stores [M or N rows][K] with the 128-byte
+// swizzle (16-byte chunks XOR row % 8), an MN-major one [K rows][M or N] with
+// the 128-byte swizzle of 32-byte atomicity (32-byte chunks XOR row % 4), the
+// only swizzle tcgen05 takes for 32-bit MN-major operands.
+// Tensor memory (512 columns): D0 [0, 64), D1 [64, 192), D2 [192, 320),
+// K~^T [320, 384).  One thread issues the MMAs and commits to one mbarrier;
+// every wait is bounded.  Rows past the sequence end are zero with g = beta
+// = 0, as the reference's padding.
+#pragma once
+
+#include "attention_sm100.cuh"
+#include "common.cuh"
+#include "gdn.cuh"
+
+namespace clef {
+
+constexpr int kGdnTcDim = 128;
+
+struct GdnTcShape {
+  static constexpr int C = kGdnChunk, DH = kGdnTcDim, LDA = C + 4;
+  static constexpr uint32_t S_BYTES = DH * DH * 4;        // state, MN-major B [dk rows][dv]
+  static constexpr uint32_t A0_BYTES = 2 * C * DH * 4;    // [k; q] then [W; q e^g], K-major [128 rows][dk]
+  static constexpr uint32_t V_BYTES = C * DH * 4;         // v beta -> U -> V_new, MN-major [tokens][dv]
+  static constexpr uint32_t AS_BYTES = C * LDA * 4;       // system matrix, row-major
+  static constexpr uint32_t MISC_FLOATS = 4 * C + 3 * DH * 4 + 2 * C;  // gates, conv taps, norm partial sums
+  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + AS_BYTES + MISC_FLOATS * 4 + 64;
+  static constexpr uint32_t D0 = 0, D1 = 64, D2 = 192, KT = 320, TMEM_COLS = 512;
+};
+
+// Byte offset of element (row, col) of a K-major fp32 operand tile (rows =
+// M or N, col = K) in atoms of `rows` rows x 32 columns, with the 128-byte
+// swizzle: the eight 16-byte chunks of a 128-byte row XOR-permuted by row % 8.
+__device__ __forceinline__ uint32_t gdn_sw(int row, int col, int rows) {
+  return static_cast<uint32_t>((col >> 5) * (rows * 128) + row * 128 + ((((col & 31) >> 2) ^ (row & 7)) << 4) +
+                               ((col & 3) << 2));
+}
+
+// The same for an MN-major fp32 operand tile (row = K, col = M or N).  For
+// 32-bit MN-major operands tcgen05 takes only the 128-byte swizzle with
+// 32-byte atomicity: the four 32-byte chunks of a 128-byte row XOR-permuted
+// by row % 4, K rows in groups of four (512 bytes).
+__device__ __forceinline__ uint32_t gdn_sw_mn(int row, int col, int rows) {
+  return static_cast<uint32_t>((col >> 5) * (rows * 128) + row * 128 + ((((col & 31) >> 3) ^ (row & 3)) << 5) +
+                               ((col & 7) << 2));
+}
+
+// Shared-memory descriptor of such an MN-major tile: `lbo` bytes between
+// 32-column atoms, 512 bytes between 4-row K groups, layout type 1
+// (SWIZZLE_128B_BASE32B), descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc_mn128_32b(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(512 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(1) << 61;
+  return d;
+}
+
+// Round to TF32 (10-bit mantissa, to nearest, ties away), the operand precision of kind::tf32.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Instruction descriptor, kind::tf32: TF32 A/B, FP32 D; a_mn / b_mn = MN-major operands.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int m, int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(a_mn) << 15) | (static_cast<uint32_t>(b_mn) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// A from tensor memory: row i of A in lane i, one TF32 per 32-bit column, K = 8 over 8 columns.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Stage L: conv + SiLU (text.py:31-39), L2 norms of q and k (reference.py:14-21)
+// for rows t0..t0+63 into the operand tiles: k -> A0 rows 0-63, q (x dk^-1/2)
+// -> A0 rows 64-127, v -> V.  The sliding-window arithmetic is gdn_load_chunk's
+// (same taps, same order of operations), only the stores differ.
+template <int W>
+__device__ __forceinline__ void gdn_tc_load_chunk(const GdnArgs& a, const __nv_bfloat16* proj,
+                                                  const __nv_bfloat16* convw, const float* wsm, long long row0, int t0,
+                                                  int q_col, int k_col, int v_col, uint8_t* sA0, uint8_t* sV) {
+  using T = __nv_bfloat16;
+  constexpr int C = kGdnChunk, DH = kGdnTcDim, VN = GdnVec<T>::N, GL = DH / VN, RPP = kGdnThreads / GL;
+  constexpr int RT = C / RPP, NX = RT + W - 1;
+  const int tid = threadIdx.x, g = tid % GL, r0 = (tid / GL) * RT;
+  const int shift = W - a.width;
+  constexpr int NK = W <= 4 ? 3 : 1;
+  uint4 raw[NK][NX];
+  auto load_kind = [&](int kind, uint4 (&dst)[NX]) {
+    const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + g * VN;
+#pragma unroll
+    for (int i = 0; i < NX; ++i) {
+      const int tt = t0 + r0 - (W - 1) + i;
+      dst[i] = (tt >= 0 && tt < a.S) ? *reinterpret_cast<const uint4*>(proj + (row0 + tt) * a.ldp + col)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  if constexpr (NK == 3) {
+#pragma unroll
+    for (int kind = 0; kind < 3; ++kind) load_kind(kind, raw[kind]);
+  }
+#pragma unroll
+  for (int kind = 0; kind < 3; ++kind) {
+    const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + g * VN;
+    if constexpr (NK == 1) load_kind(kind, raw[0]);
+    const uint4 (&rk)[NX] = raw[NK == 3 ? kind : 0];
+    float w[VN][W];
+#pragma unroll
+    for (int c = 0; c < VN; ++c)
+#pragma unroll
+      for (int i = 0; i < W; ++i)
+        w[c][i] = wsm ? wsm[(kind * DH + g * VN + c) * W + i]
+                      : (i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f);
+    float x[NX][VN];
+#pragma unroll
+    for (int i = 0; i < NX; ++i) {
+      const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&rk[i]);
+#pragma unroll
+      for (int c = 0; c < VN; ++c) x[i][c] = __bfloat162float(hv[c]);
+    }
+#pragma unroll
+    for (int j = 0; j < RT; ++j) {
+      const int r = r0 + j;
+      float y[VN];
+#pragma unroll
+      for (int c = 0; c < VN; ++c) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(x[j + i][c], w[c][i]));
+        const float z = round_to<T>(acc);
+        y[c] = t0 + r < a.S ? round_to<T>(z * sigmoid_fast(z)) : 0.f;
+      }
+      if (kind < 2) {
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < VN; ++c) ss += y[c] * y[c];
+        const float inv = rsqrtf(group_sum<GL>(ss) + 1e-6f);
+        const float scale = kind == 0 ? a.qscale : 1.f;
+#pragma unroll
+        for (int c = 0; c < VN; ++c) y[c] = round_to<T>(y[c] * inv) * scale;
+        if (kind == 0) {  // q x dk^-1/2 is an MMA operand: TF32 (k is bf16, exact in TF32)
+#pragma unroll
+          for (int c = 0; c < VN; ++c) y[c] = to_tf32(y[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < VN; c += 4) {
+        const float4 v4 = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
+        if (kind == 2)
+          *reinterpret_cast<float4*>(sV + gdn_sw_mn(r, g * VN + c, C)) = v4;
+        else
+          *reinterpret_cast<float4*>(sA0 + gdn_sw(kind == 0 ? C + r : r, g * VN + c, 2 * C)) = v4;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
+  using Sh = GdnTcShape;
+  using T = __nv_bfloat16;
+  constexpr int C = Sh::C, DH = Sh::DH, LDA = Sh::LDA;
+  constexpr uint32_t IDESC_G = idesc_tf32_f32(128, C, false, false);     // A0 k^T: both K-major
+  constexpr uint32_t IDESC_S = idesc_tf32_f32(128, DH, false, true);     // A0 S: S is MN-major
+  constexpr uint32_t IDESC_V = idesc_tf32_f32(128, DH, false, true);     // (tmem A) V_new: V_new is MN-major
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sS = smem;
+  uint8_t* sA0 = sS + Sh::S_BYTES;
+  uint8_t* sV = sA0 + Sh::A0_BYTES;
+  float* As = reinterpret_cast<float*>(sV + Sh::V_BYTES);  // [C][LDA]
+  float* gs = As + C * LDA;                                // cumulative g
+  float* bs = gs + C;                                      // beta
+  float* es = bs + C;                                      // e^g
+  float* ws = es + C;                                      // e^(g_last - g)
+  float* wconv = ws + C;                                   // [3][DH][4] conv taps (width <= 4)
+  float* red = wconv + 3 * DH * 4;                         // [2][C] output-row partial sums of squares
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(red + 2 * C);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+  int* fail = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;  // tensor-memory lane quarter, column half
+  const int lrow = quarter * 32 + lane;            // this thread's tensor-memory lane
+  const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
+  const int hk = h / (a.nv / a.nh);
+  const T* proj = static_cast<const T*>(a.proj);
+  const T* convw = static_cast<const T*>(a.conv);
+  const T* nw = static_cast<const T*>(a.norm_w);
+  T* out = static_cast<T*>(a.out);
+  const float neg_a = -expf(to_f32(static_cast<const T*>(a.A_log)[h]));
+  const float dt_bias = to_f32(static_cast<const T*>(a.dt_bias)[h]);
+  const long long row0 = static_cast<long long>(b) * a.S;
+  const int q_col = hk * DH, k_col = a.k_col + hk * DH, v_col = a.v_col + h * DH;
+
+  if (tid == 0) {
+    mbar_init(mma_bar, 1);
+    *fail = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, Sh::TMEM_COLS);
+    tmem_relinquish();
+  }
+  for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
+  if (a.width <= 4) {
+    const int shift = 4 - a.width;
+    for (int i = tid; i < 3 * DH * 4; i += kGdnThreads) {
+      const int kind = i / (DH * 4), c = (i / 4) % DH, tap = i % 4;
+      const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + c;
+      wconv[i] = tap >= shift ? to_f32(convw[static_cast<long long>(col) * a.width + (tap - shift)]) : 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  uint32_t mma_phase = 0;
+
+  // One thread issues a group of MMAs and commits; everyone waits for it.
+  auto mma_wait = [&]() -> bool {
+    const bool ok = mbar_wait(mma_bar, mma_phase, a.status, kTimeoutMma);
+    mma_phase ^= 1;
+    tc_fence_after();
+    return __syncthreads_and(ok) != 0;
+  };
+
+  const uint32_t a0 = smem_u32(sA0), sv = smem_u32(sV), ss_addr = smem_u32(sS);
+  const int chunks = (a.S + C - 1) / C;
+  for (int ci = 0; ci < chunks; ++ci) {
+    const int t0 = ci * C;
+    // ---- L: conv + SiLU, L2 norms, gates ----
+    if (a.width <= 4)
+      gdn_tc_load_chunk<4>(a, proj, convw, wconv, row0, t0, q_col, k_col, v_col, sA0, sV);
+    else
+      gdn_tc_load_chunk<8>(a, proj, convw, nullptr, row0, t0, q_col, k_col, v_col, sA0, sV);
+    if (tid < C) {
+      const int t = t0 + tid;
+      if (t < a.S) {
+        const T* pr = proj + (row0 + t) * a.ldp;
+        gs[tid] = neg_a * softplus_f(to_f32(pr[a.a_col + h]) + dt_bias);
+        bs[tid] = round_to<T>(sigmoid_fast(to_f32(pr[a.b_col + h])));
+      } else {
+        gs[tid] = 0.f;
+        bs[tid] = 0.f;
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+    // cumulative gate (sequential, as cumsum) and its exponentials; M0 meanwhile
+    if (warp == 0) {
+      if (lane == 0) {
+        float acc = 0.f;
+        for (int r = 0; r < C; ++r) {
+          acc += gs[r];
+          gs[r] = acc;
+        }
+      }
+      __syncwarp();
+      const float last = gs[C - 1];
+      for (int r = lane; r < C; r += 32) {
+        es[r] = expf(gs[r]);
+        ws[r] = expf(last - gs[r]);
+      }
+    }
+    if (tid == 32) {
+      // ---- M0: D0 = [k; q] k^T (the k operand values are exact in TF32: bf16 after the norm) ----
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < DH / 8; ++kk) {
+        const uint32_t off = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
+        umma_tf32(tmem + Sh::D0, smem_desc_k128(a0 + off), smem_desc_k128(a0 + off), IDESC_G, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(mma_bar);
+    }
+    if (!mma_wait()) break;
+    // ---- P: system matrix, M, q e^g, K~^T ----
+    {
+      // this thread: tensor-memory lane lrow, D0 columns [32 half, +32)
+      uint32_t d[32];
+      tmem_ld32(tmem + t_lane + Sh::D0 + 32 * half, d);
+      tmem_wait_ld();
+      if (lrow < C) {
+        const int i = lrow;
+        const float gi = gs[i], bi = bs[i];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = 32 * half + e;
+          As[i * LDA + j] = j < i ? -(__uint_as_float(d[e]) * bi) * exp_fast(gi - gs[j]) : 0.f;
+        }
+      } else {
+        const int i = lrow - C;
+        const float gi = gs[i];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = 32 * half + e;
+          d[e] = __float_as_uint(j <= i ? to_tf32(__uint_as_float(d[e]) * exp_fast(gi - gs[j])) : 0.f);
+        }
+        tmem_st32(tmem + t_lane + Sh::D0 + 32 * half, d);
+      }
+      // K~^T: lane i (key dim) x columns c in [32 half, +32): k[c][i] e^{g_last - g_c}
+      uint32_t kt[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int c = 32 * half + e;
+        kt[e] = __float_as_uint(to_tf32(*reinterpret_cast<const float*>(sA0 + gdn_sw(c, lrow, 2 * C)) * ws[c]));
+      }
+      tmem_st32(tmem + t_lane + Sh::KT + 32 * half, kt);
+      tmem_wait_st();
+      // q -> q e^g (rows 64-127 of A0), rounded to TF32
+      for (int idx = tid; idx < C * DH; idx += kGdnThreads) {
+        const int r = idx / DH, col = idx % DH;
+        float* p = reinterpret_cast<float*>(sA0 + gdn_sw(C + r, col, 2 * C));
+        *p = to_tf32(*p * es[r]);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    // ---- T: (I - A) X = [v beta | k beta e^g], one column per thread, in place ----
+    {
+      const bool vcol = tid < DH;
+      const int col = vcol ? tid : tid - DH;
+      float x[C];
+#pragma unroll
+      for (int r = 0; r < C; ++r) {
+        float* p = reinterpret_cast<float*>(vcol ? sV + gdn_sw_mn(r, col, C) : sA0 + gdn_sw(r, col, 2 * C));
+        float acc = vcol ? *p * bs[r] : *p * bs[r] * es[r];
+#pragma unroll
+        for (int j4 = 0; j4 + 4 <= r; j4 += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(As + r * LDA + j4);
+          acc = fmaf(a4.x, x[j4], acc);
+          acc = fmaf(a4.y, x[j4 + 1], acc);
+          acc = fmaf(a4.z, x[j4 + 2], acc);
+          acc = fmaf(a4.w, x[j4 + 3], acc);
+        }
+#pragma unroll
+        for (int j = r & ~3; j < r; ++j) acc = fmaf(As[r * LDA + j], x[j], acc);
+        x[r] = acc;
+        *p = vcol ? acc : to_tf32(acc);  // U stays FP32; W becomes an operand
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- M1: D1 = [W; q e^g] S ----
+    if (tid == 32) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < DH / 8; ++kk) {
+        const uint32_t aoff = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
+        umma_tf32(tmem + Sh::D1, smem_desc_k128(a0 + aoff), smem_desc_mn128_32b(ss_addr + kk * 1024, DH * 128),
+                  IDESC_S, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(mma_bar);
+    }
+    if (!mma_wait()) break;
+    // ---- V: V_new = U - W S (rows 0-63), in place of U ----
+    if (lrow < C) {
+      const int c = lrow;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t d[32];
+        const int j0 = 64 * half + 32 * part;
+        tmem_ld32(tmem + t_lane + Sh::D1 + j0, d);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          float4* p = reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e, C));
+          float4 u = *p;
+          u.x = to_tf32(u.x - __uint_as_float(d[e]));
+          u.y = to_tf32(u.y - __uint_as_float(d[e + 1]));
+          u.z = to_tf32(u.z - __uint_as_float(d[e + 2]));
+          u.w = to_tf32(u.w - __uint_as_float(d[e + 3]));
+          *p = u;
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---- M2: D1 += [. ; M] V_new;  M3: D2 = K~^T V_new ----
+    if (tid == 32) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < C / 8; ++kk) {
+        const uint64_t bdesc = smem_desc_mn128_32b(sv + kk * 1024, C * 128);
+        umma_tf32_ts(tmem + Sh::D1, tmem + Sh::D0 + kk * 8, bdesc, IDESC_V, 1u);
+        umma_tf32_ts(tmem + Sh::D2, tmem + Sh::KT + kk * 8, bdesc, IDESC_V, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(mma_bar);
+    }
+    if (!mma_wait()) break;
+    // ---- S = S e^{g_last} + D2 (lane i = key dim, 64 value columns per thread) ----
+    {
+      const float decay = es[C - 1];
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t d[32];
+        const int j0 = 64 * half + 32 * part;
+        tmem_ld32(tmem + t_lane + Sh::D2 + j0, d);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          float4* p = reinterpret_cast<float4*>(sS + gdn_sw_mn(lrow, j0 + e, DH));
+          float4 s = *p;
+          s.x = to_tf32(fmaf(s.x, decay, __uint_as_float(d[e])));
+          s.y = to_tf32(fmaf(s.y, decay, __uint_as_float(d[e + 1])));
+          s.z = to_tf32(fmaf(s.z, decay, __uint_as_float(d[e + 2])));
+          s.w = to_tf32(fmaf(s.w, decay, __uint_as_float(d[e + 3])));
+          *p = s;
+        }
+      }
+    }
+    // ---- O: gated RMSNorm x SiLU(z) of the output rows (text.py:61-67) ----
+    if (lrow >= C) {
+      const int c = lrow - C, t = t0 + c;
+      float o[64];
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t d[32];
+        tmem_ld32(tmem + t_lane + Sh::D1 + 64 * half + 32 * part, d);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[32 * part + e] = round_to<T>(__uint_as_float(d[e]));
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) ss += o[e] * o[e];
+      red[half * C + c] = ss;
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 2, 3, 6, 7
+      const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
+      if (t < a.S) {
+        const T* zrow = proj + (row0 + t) * a.ldp + a.z_col + h * DH + 64 * half;
+        T* orow = out + (row0 + t) * a.ldo + h * DH + 64 * half;
+#pragma unroll
+        for (int e8 = 0; e8 < 64; e8 += 8) {
+          GdnVec<T> z, wv, res;
+          z.load(zrow + e8);
+          wv.load(nw + 64 * half + e8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float n = round_to<T>(round_to<T>(o[e8 + e] * rs) * wv.v[e]);
+            res.v[e] = n * (z.v[e] * sigmoid_fast(z.v[e]));
+          }
+          res.store(orow + e8);
+        }
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, Sh::TMEM_COLS);
+}
+
+}  // namespace clef

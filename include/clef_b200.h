@@ -154,8 +154,23 @@ int clef_forward_head(void* handle, const ClefBatch* batch, const float* hidden,
  * workspace for this shape exists (see clef_reserve). */
 int clef_forward_device(void* handle, const ClefBatch* batch, float* out_logits, void* stream);
 
-/* Allocate the workspace for batches up to (b, s, lx, o, q) ahead of time. */
+/* Allocate the workspace for batches up to (b, s, lx, o, q) ahead of time:
+ * the device buffers of a forward and the pinned host staging of
+ * clef_forward (under TP, also the exchange of the ranks' peer-memory
+ * handles, so every rank must call it with the same shape).  Sizes only grow;
+ * a later forward within every reserved maximum allocates nothing.  A
+ * serving warm-up calls it for the largest batch it admits -- the
+ * counterpart of the reference server's warm-up request
+ * (serve/app.py:385-406), which the library turns into one reservation of
+ * the whole admitted range instead of one small shape. */
 int clef_reserve(void* handle, int b, int s, int lx, int o, int q);
+
+/* Number of workspace allocations since clef_create: device buffers grown,
+ * pinned staging grown, and TP peer-handle exchanges (each follows a move of
+ * the buffers peers write into).  Lets a caller check that its warm-up
+ * reserved enough.  No counterpart in the reference (XLA allocates inside
+ * each jitted call). */
+int clef_workspace_allocations(void* handle, int64_t* count);
 
 /* Synchronise the device and report (then clear) any device-side status a
  * kernel recorded since the last check (CLEF_EDEVICE: wait timeout or an
@@ -216,7 +231,8 @@ int clef_op_gemm_qkv(const void* A, const void* B, void* out, int M, int K, int 
 int clef_op_rmsnorm(int dtype, const void* x, const void* w, void* out, int rows, int dim, float eps, void* stream);
 
 /* In-place per-head q/k RMSNorm + partial RoPE on a packed projection
- * [b*s, Hq*2d + 2*Hkv*d] (models/qwen3_5/text.py:79-88, nn.py:31-44). */
+ * [b*s, Hq*2d + 2*Hkv*d] (models/qwen3_5/text.py:79-88, nn.py:31-44).
+ * head_dim <= 1536. */
 int clef_op_qk_norm_rope(int dtype, void* qkv, int b, int s, int hq, int hkv, int d, float partial_rotary_factor,
                          float rope_theta, const void* q_norm, const void* k_norm, float eps, void* stream);
 
@@ -228,11 +244,14 @@ int clef_op_qk_norm_rope(int dtype, void* qkv, int b, int s, int hq, int hkv, in
  * arguments and result as clef_op_qk_norm_rope; the cos/sin tables live in a
  * fixed 8 MiB array inside the library (held on every GPU that loads it until
  * exit) instead of memory allocated per call.
- *  - Limit: s * rot/2 <= 1048576 table entries and rot/2 <= 128
- *    (rot = head_dim * partial_rotary_factor); larger sizes return CLEF_EINVAL.
- *  - The first call on each device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
+ *  - Limit: s * rot/2 <= 1048576 table entries, rot/2 <= 128 and
+ *    head_dim <= 1536 (rot = head_dim * partial_rotary_factor); larger sizes
+ *    return CLEF_EINVAL before any device work.
+ *  - Each call outside stream capture looks up the array's device address
+ *    (cudaGetSymbolAddress) with the device current, so a context that was
+ *    reset and rebuilt gets its new address; the first such lookup on a
+ *    device loads the module there.  Make one call on each device before any
+ *    stream capture: during capture the last address looked up is used.
  *  - Every call rewrites the table entries it reads, so no state carries over
  *    between calls, but all calls on a device share the one array: calls whose
  *    kernels overlap on the GPU (e.g. on two streams) race. */

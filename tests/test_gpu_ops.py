@@ -275,9 +275,10 @@ def test_attention_bf16_flash(d, s):
 
 @pytest.mark.parametrize("d", [128, 256])
 def test_attention_bf16_long_rows_with_rescales(d):
-    """Many 64-key tiles per query tile, scores large enough that the running
-    max moves by more than the lazy-rescale margin (head_dim 128 keeps P in
-    tensor memory; 256 in shared memory)."""
+    """Many key tiles per query tile, scores large enough that the running
+    max moves by more than the lazy-rescale margin (head_dim 128: one CTA,
+    64-key tiles; 256: CTA pairs, 128-key tiles; both keep P in tensor
+    memory)."""
     got, expected = attention_case("bf16", d, 1024, lengths=[1024, 700], qscale=6.0, seed=3)
     np.testing.assert_allclose(got, expected, rtol=2e-2, atol=2e-2)
     assert np.abs(got - expected).mean() < 2e-3
@@ -289,14 +290,25 @@ def test_attention_fp32_exact(d):
     np.testing.assert_allclose(got, expected, rtol=1e-4, atol=1e-5)
 
 
-@pytest.mark.parametrize("dtype,d", [("bf16", 64), ("bf16", 128), ("fp32", 64)])
+@pytest.mark.parametrize("s,lengths", [(384, [384, 300]), (2048, [2048, 1999])])
+def test_attention_bf16_d256_pair_tiles(s, lengths):
+    """head_dim 256 runs on CTA pairs over 256 query rows: a sequence of 384
+    leaves the second CTA of the last pair past the end (it must store
+    nothing) while every 128-row tile leaves through TMA stores; 2048 is the
+    benchmark layer's length."""
+    got, expected = attention_case("bf16", 256, s, lengths=lengths, seed=5)
+    np.testing.assert_allclose(got, expected, rtol=2e-2, atol=2e-2)
+    assert np.abs(got - expected).mean() < 2e-3
+
+
+@pytest.mark.parametrize("dtype,d", [("bf16", 64), ("bf16", 128), ("bf16", 256), ("fp32", 64)])
 def test_attention_beyond_reference_flags(dtype, d):
     got, expected = attention_case(dtype, d, 200, softcap=5.0, window=48)
     tol = dict(rtol=2e-2, atol=2e-2) if dtype == "bf16" else dict(rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(got, expected, **tol)
 
 
-@pytest.mark.parametrize("dtype,d", [("bf16", 64), ("bf16", 128), ("fp32", 64)])
+@pytest.mark.parametrize("dtype,d", [("bf16", 64), ("bf16", 128), ("bf16", 256), ("fp32", 64)])
 def test_attention_length_one_row(dtype, d):
     """A state whose only valid key is key 0: every later query attends to it alone."""
     got, expected = attention_case(dtype, d, 66, lengths=[1, 66])
