@@ -20,7 +20,15 @@ events inside the timed region.  ``cpu_baseline`` = the CPU oracle (FP32,
 the reference's impl="auto" arithmetic) on a bounded sample, extrapolated.
 
 With torchrun (N > 1) every rank holds a full replica and runs its own batch
-(data parallel, no collective on the data path): ``scaling`` is "weak".
+(data parallel, no collective on the data path): ``value`` scales "weak".
+The same line then carries ``tp``: cfg2 tensor-parallel over the N ranks
+(heads and MLP columns sharded, FP32 partials of o-proj and down-proj summed
+over NVLink peer memory), one shared batch per step (strong scaling), with
+its per-category device time split into GEMM, attention, reduction and
+barrier; and ``tp_parity``: a TP=N check of small sharded models against the
+CPU oracle, run before anything is timed.  At N = 1 the line carries
+``parity``: a two-layer slice of the cfg2 model (same dims, BF16, one
+2048-token state) against the CPU oracle, also outside the timed region.
 """
 
 from __future__ import annotations
@@ -220,6 +228,136 @@ def make_batch(seed: int) -> dict[str, np.ndarray]:
 
 
 # ---------------------------------------------------------------------------
+# parity checks outside the timed region (the CPU oracle is the checker)
+# ---------------------------------------------------------------------------
+
+PARITY_SEED = 11
+
+
+def probability_agreement(actual: np.ndarray, expected: np.ndarray, arrays) -> tuple[float, int, int]:
+    """(max abs option-probability error, fields whose argmax differs while the
+    expected top-2 gap is at least 1e-3, fields compared): the north star's
+    BF16 bar (probabilities within 1e-2, identical choices unless the
+    reference's top-2 gap is below 1e-3), on the per-field softmax of
+    models/clef/input.py:185-192."""
+    from deciax_b200.synthetic import field_probabilities
+
+    err, flips, fields = 0.0, 0, 0
+    for fa, fe in zip(field_probabilities(actual, arrays), field_probabilities(expected, arrays)):
+        for a, e in zip(fa, fe):
+            fields += 1
+            err = max(err, float(np.abs(a - e).max()))
+            if a.argmax() != e.argmax():
+                top = np.sort(e)[::-1]
+                if len(top) < 2 or top[0] - top[1] >= 1e-3:
+                    flips += 1
+    return err, flips, fields
+
+
+def cfg2_slice_parity(device: int, layers: int = 2, lengths: tuple[int, ...] = (SEQ,), seed: int = PARITY_SEED,
+                      oracle_floor: bool = True) -> dict:
+    """The CUDA forward against the CPU oracle on a slice of the bench
+    workload: ``layers`` decoder layers at cfg2's dims (D3584, 16q/8kv x 256,
+    F14336, V256000), BF16, the bench's joint head, states of ``lengths``
+    real tokens in the 2048 bucket with 4 choice x 4 options each.
+
+    Weights are drawn on the GPU as ``build_model`` draws them (torch RNG,
+    N(0, 0.02)), uploaded, and copied back for the oracle; the oracle gets
+    only the embedding rows the batch uses (ids remapped), which gathers the
+    same vectors.  Runs outside any timed region.  With ``oracle_floor`` the
+    oracle runs a second time with float64 accumulation in its linear layers;
+    the probability distance between its two runs is reported beside the
+    CUDA path's, as the drift expected between two faithful BF16
+    implementations at these dims."""
+    import torch
+
+    from deciax_b200.config import HeadConfig, TextConfig
+    from deciax_b200.model import ClefCudaModel
+    from deciax_b200.synthetic import BatchSpec, synthetic_batch, synthetic_head_weights
+    from oracle import clef_oracle as O
+
+    t0 = time.perf_counter()
+    cfg = dict(CFG2, num_layers=layers)
+    config = TextConfig.full_attention(**cfg)
+    head = HeadConfig(**HEAD)
+    D, F, hq, hkv, d, V = (cfg[k] for k in ("hidden_size", "intermediate_size", "num_attention_heads", "num_key_value_heads", "head_dim", "vocab_size"))
+    model = ClefCudaModel(config, head, dtype="bf16", device=device, max_seq_len=SEQ)
+    gen = torch.Generator(device=f"cuda:{device}")
+    gen.manual_seed(seed)
+
+    def randn(*shape):
+        return torch.empty(shape, dtype=torch.bfloat16, device=f"cuda:{device}").normal_(0.0, WEIGHT_STD, generator=gen)
+
+    def host(t) -> np.ndarray:
+        return t.float().cpu().numpy()
+
+    arrays = synthetic_batch(BatchSpec(states=len(lengths), seq=SEQ, questions=QUESTIONS, options_per_question=OPTIONS,
+                                       lengths=tuple(lengths)), V, seed)
+    used = np.unique(np.concatenate([arrays["input_ids"].ravel(), arrays["lexical_ids"].ravel()]))
+    emb = randn(V, D)
+    model.upload_device("embedding", emb)
+    model.upload_device("lm_head", emb)
+    table = host(emb[torch.from_numpy(used.astype(np.int64)).to(emb.device)])
+    del emb
+    norm = randn(D)
+    model.upload_device("norm", norm)
+    top = {"embedding": table, "lm_head": table, "norm": host(norm)}
+    shapes = {
+        "input_layernorm.weight": (D,), "post_attention_layernorm.weight": (D,), "mixer.q_proj.weight": (hq * 2 * d, D),
+        "mixer.k_proj.weight": (hkv * d, D), "mixer.v_proj.weight": (hkv * d, D), "mixer.o_proj.weight": (D, hq * d),
+        "mixer.q_norm.weight": (d,), "mixer.k_norm.weight": (d,), "mlp.gate_proj.weight": (F, D),
+        "mlp.up_proj.weight": (F, D), "mlp.down_proj.weight": (D, F),
+    }
+    host_layers = []
+    for i in range(layers):
+        p = {}
+        for name, shape in shapes.items():
+            w = randn(*shape)
+            model.upload_device(f"layers.{i}.{name}", w)
+            p[name] = host(w)
+        host_layers.append(p)
+    hp = synthetic_head_weights(D, head, seed=seed, std=WEIGHT_STD, dtype="bf16")
+    for k, v in hp.items():
+        model.upload("head." + k, v)
+    model.finalize()
+    logits, hidden = model.forward_with_hidden(arrays)
+    model.close()
+    torch.cuda.empty_cache()
+    t1 = time.perf_counter()
+    oracle_arrays = dict(arrays)
+    oracle_arrays["input_ids"] = np.searchsorted(used, arrays["input_ids"]).astype(np.int32)
+    oracle_arrays["lexical_ids"] = np.searchsorted(used, arrays["lexical_ids"]).astype(np.int32)
+    oc = O.TextConfig(hidden_size=D, intermediate_size=F, num_attention_heads=hq, num_key_value_heads=hkv, head_dim=d,
+                      layer_types=config.layer_types)
+    hp32 = {k: np.asarray(v, np.float32) for k, v in hp.items()}
+    expected, exp_hidden = O.forward(top, host_layers, hp32, oracle_arrays, oc,
+                                     O.HeadConfig(heads=HEAD["heads"], routing_layers=HEAD["routing_layers"],
+                                                  layers=HEAD["layers"]), "bf16", return_hidden=True)
+    t2 = time.perf_counter()
+    err, flips, fields = probability_agreement(logits, expected, arrays)
+    valid = arrays["mask"]
+    diff = np.abs(hidden[valid] - exp_hidden[valid]) / np.abs(exp_hidden[valid]).max()
+    floor = None
+    if oracle_floor:
+        # the same restatement with float64 accumulation in every linear layer:
+        # how far two faithful implementations drift apart on this case
+        with O.matmul_accumulation(np.float64):
+            alt = O.forward(top, host_layers, hp32, oracle_arrays, oc,
+                            O.HeadConfig(heads=HEAD["heads"], routing_layers=HEAD["routing_layers"], layers=HEAD["layers"]),
+                            "bf16")
+        floor = probability_agreement(alt, expected, arrays)[0]
+    return {
+        "case": f"cfg2 dims, {layers} layers, BF16, {len(lengths)} state(s) of {list(lengths)} tokens (bucket {SEQ}), "
+        f"{QUESTIONS} choice x {OPTIONS} options, weights seed {seed}",
+        "max_prob_err": err, "argmax_flips": flips, "fields": fields, "prob_tol": 1e-2,
+        "oracle_fp64_accumulation_prob_err": floor,
+        "hidden_err_max_rel": float(diff.max()), "hidden_err_mean_rel": float(diff.mean()),
+        "ok": bool(err < 1e-2 and flips == 0 and np.isfinite(logits[arrays["option_mask"]]).all()),
+        "gpu_seconds": round(t1 - t0, 2), "oracle_seconds": round(t2 - t1, 2),
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline: the oracle (FP32) on a bounded sample
 # ---------------------------------------------------------------------------
 
@@ -291,6 +429,175 @@ def reference_arm(args) -> None:
 # ---------------------------------------------------------------------------
 
 
+TP_PREFLIGHT_BATCH = dict(states=3, seq=256, questions=2, options_per_question=3, lengths=(256, 130, 40), row_bucket=4)
+
+
+def tp_preflight_config(kind: str):
+    """Small models that shard at TP = 2, 4 and 8 (16 query / 8 key-value
+    heads; Gated DeltaNet 8 key / 16 value heads).  Intermediate 12288 makes
+    the down-proj run the fused GEMM + peer reduction at every tp in BF16
+    (K tp / (tp - 1) >= 1536), the o-proj fused at TP=2 and unfused at 4 and 8."""
+    from deciax_b200.config import HeadConfig, TextConfig
+
+    head = HeadConfig(heads=4, routing_layers=1, layers=1, width=64, ffn=128)
+    dims = dict(hidden_size=1024, intermediate_size=12288, num_attention_heads=16, num_key_value_heads=8, head_dim=128)
+    if kind == "mixed":
+        return TextConfig(**dims, linear_num_key_heads=8, linear_num_value_heads=16, linear_key_head_dim=64,
+                          linear_value_head_dim=64, linear_conv_kernel_dim=4,
+                          layer_types=("linear_attention", "full_attention"), rms_norm_eps=1e-6, rope_theta=10000.0,
+                          partial_rotary_factor=0.25, vocab_size=1000), head
+    return TextConfig.full_attention(**dims, num_layers=2, vocab_size=1000), head
+
+
+def tp_preflight(rank: int, world: int, local: int) -> dict | None:
+    """TP = world parity before the timed region: each small model of
+    ``tp_preflight_config`` in FP32 and BF16, sharded over the ranks, runs one
+    forward of a ragged 3-state batch; rank 0 checks its logits and hidden
+    states against the CPU oracle (FP32: hidden within 1e-4 relative, logits
+    within 1e-4; BF16: option probabilities within 1e-2, no argmax flip)
+    and that every rank ends with the same bits.  Returns the summary on
+    rank 0, None elsewhere."""
+    import torch.distributed as dist
+
+    from deciax_b200.model import ClefCudaModel
+    from deciax_b200.synthetic import BatchSpec, synthetic_batch, synthetic_weights
+
+    cases, ok = {}, True
+    for kind in ("full", "mixed"):
+        for dtype in ("fp32", "bf16"):
+            config, head = tp_preflight_config(kind)
+            top, layers, hp = synthetic_weights(config, head, seed=5, embed_std=1.0, dtype=dtype)
+            nccl_id = share_from_rank0(nccl_unique_id)
+            model = ClefCudaModel.from_arrays(config, head, top, layers, hp, dtype=dtype, device=local, tp_rank=rank,
+                                              tp_size=world, nccl_id=nccl_id, max_seq_len=256, tp_timeout=300.0)
+            arrays = synthetic_batch(BatchSpec(**TP_PREFLIGHT_BATCH), config.vocab_size, seed=6)
+            logits, hidden = model.forward_with_hidden(arrays)
+            model.close()
+            gathered = [None] * world
+            dist.all_gather_object(gathered, (logits, hidden))
+            if rank != 0:
+                continue
+            from oracle import clef_oracle as O
+
+            f32 = lambda t: {k: np.asarray(v, np.float32) for k, v in t.items()}  # noqa: E731
+            oc = O.TextConfig(
+                hidden_size=config.hidden_size, intermediate_size=config.intermediate_size,
+                num_attention_heads=config.num_attention_heads, num_key_value_heads=config.num_key_value_heads,
+                head_dim=config.head_dim, layer_types=config.layer_types, linear_num_key_heads=config.linear_num_key_heads,
+                linear_num_value_heads=config.linear_num_value_heads, linear_key_head_dim=config.linear_key_head_dim,
+                linear_value_head_dim=config.linear_value_head_dim, linear_conv_kernel_dim=config.linear_conv_kernel_dim)
+            exp_logits, exp_hidden = O.forward(f32(top), [f32(p) for p in layers], f32(hp), arrays, oc,
+                                               O.HeadConfig(heads=head.heads, routing_layers=head.routing_layers,
+                                                            layers=head.layers), dtype, return_hidden=True)
+            valid, m = arrays["mask"], arrays["option_mask"]
+            same = all(np.array_equal(g[0], logits) and np.array_equal(g[1][valid], hidden[valid]) for g in gathered)
+            entry = {"ranks_identical": bool(same)}
+            if dtype == "fp32":
+                scale = float(np.abs(exp_hidden[valid]).max())
+                h_ratio = float((np.abs(hidden[valid] - exp_hidden[valid]) / (1e-4 * scale + 1e-4 * np.abs(exp_hidden[valid]))).max())
+                l_ratio = float((np.abs(logits[m] - exp_logits[m]) / (1e-4 + 1e-4 * np.abs(exp_logits[m]))).max())
+                entry |= {"hidden_err_over_tol": h_ratio, "logit_err_over_tol": l_ratio, "tol": "rtol 1e-4, atol 1e-4 x max|h|"}
+                entry["ok"] = bool(h_ratio <= 1 and l_ratio <= 1 and same)
+            else:
+                err, flips, fields = probability_agreement(logits, exp_logits, arrays)
+                entry |= {"max_prob_err": err, "argmax_flips": flips, "fields": fields, "tol": 1e-2}
+                entry["ok"] = bool(err < 1e-2 and flips == 0 and same)
+            cases[f"{kind}-{dtype}"] = entry
+            ok &= entry["ok"]
+    if rank != 0:
+        return None
+    return {"tp": world, "case": "D1024, 16q/8kv x128, F12288, 2 layers (full: 2 full-attention; mixed: Gated DeltaNet "
+            "8 key/16 value heads x64 + full attention); 3 states of 256/130/40 tokens in 4 rows", "cases": cases, "ok": ok}
+
+
+def device_batch(arrays):
+    """The collated arrays as CUDA tensors (int32; masks as uint8)."""
+    import torch
+
+    from deciax_b200 import _lib
+
+    return {k: torch.from_numpy(np.ascontiguousarray(arrays[k]).astype(np.uint8 if arrays[k].dtype == bool else np.int32)).cuda()
+            for k in _lib.BATCH_KEYS}
+
+
+def timed_forwards(model, tensors, out, stream, steps: int, warmup: int, local: int, dist) -> tuple[float, dict, dict]:
+    """W untimed forwards, then exactly K forwards between a barrier and a
+    device synchronisation on both sides, timed with CUDA events on the
+    launching stream (the library enqueues on it); returns (ms for the K
+    forwards, per-category timeline, clocks sampled during them)."""
+    import torch
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(warmup):
+        model.forward_device(tensors, out, stream.cuda_stream)
+    torch.cuda.synchronize()
+    model.check_status()
+    barrier()
+    model.set_timing(True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(steps):
+            model.forward_device(tensors, out, stream.cuda_stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = start.elapsed_time(end)
+    timing = model.timing_report()
+    model.set_timing(False)
+    model.check_status()
+    return elapsed_ms, timing, clocks.summary()
+
+
+def tp_arm(args, rank: int, world: int, local: int, dist) -> dict:
+    """cfg2 tensor-parallel over the ``world`` ranks (heads and MLP columns
+    sharded, the o-proj and down-proj FP32 partials reduced over NVLink peer
+    memory), every rank running the same 8 x 2048 batch: strong scaling, the
+    group's tokens/s.  Returns the ``tp`` object of the bench line."""
+    import torch
+
+    from deciax_b200.synthetic import field_probabilities
+
+    model = build_model(local, tp_rank=rank, tp_size=world, nccl_id=share_from_rank0(nccl_unique_id))
+    arrays = make_batch(seed=100)
+    tensors = device_batch(arrays)
+    out = torch.empty(arrays["option_mask"].shape, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    elapsed_ms, timing, clocks = timed_forwards(model, tensors, out, stream, args.steps, args.warmup, local, dist)
+    logits = out.cpu().numpy()
+    launches = model.last_launch_count * args.steps
+    model.close()
+    if not np.isfinite(logits[arrays["option_mask"]]).all():
+        raise SystemExit("non-finite logits (tensor parallel)")
+    ms = rank_reduce(elapsed_ms, "max") / args.steps
+    tokens = STATES * SEQ
+    linear, attention, _ = algorithmic_flops(CFG2, [SEQ] * STATES)
+    peaks = measured_peaks()
+    per = {k: ms_ / args.steps for k, (ms_, n) in timing.items() if n}
+    gemm = sum(per.get(k, 0.0) for k in ("gemm_qkv", "gemm_o", "gemm_gate_up", "gemm_down"))
+    decisions = sum(len(f) for f in field_probabilities(logits, arrays))
+    return {
+        "tp": world, "value": tokens / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "scaling": "strong",
+        "decisions_per_s": decisions / (ms / 1e3),
+        "tensor_frac": {"achieved_tflops": (linear + attention) / (ms / 1e3) / 1e12,
+                        "frac_of_measured_burst_x_gpus": (linear + attention) / (ms / 1e3) / 1e12 / (peaks["bf16_tflops"] * world)},
+        "kernel_ms_per_step_rank0": {k: round(v, 3) for k, v in per.items()},
+        "split_ms_per_step_rank0": {
+            "gemm_incl_fused_reduction": round(gemm, 3), "attention": round(per.get("attention", 0.0), 3),
+            "reduction_unfused": round(per.get("residual_add", 0.0), 3), "barrier": round(per.get("allreduce", 0.0), 3),
+            "other": round(sum(per.values()) - gemm - per.get("attention", 0.0) - per.get("residual_add", 0.0)
+                           - per.get("allreduce", 0.0), 3)},
+        "gpu_launches_rank0": launches, "clocks_rank0": clocks,
+        "layout": "Hq/tp query and Hkv/tp key-value heads, F/tp MLP columns per rank; FP32 partials of o-proj and "
+        "down-proj summed over NVLink peer memory (fused into the down-proj GEMM; o-proj fused when K tp/(tp-1) >= 1536)",
+    }
+
+
 def gpu_arm(args) -> None:
     import torch
 
@@ -309,48 +616,32 @@ def gpu_arm(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     from deciax_b200 import _lib
+    from deciax_b200.build import build as build_lib
     from deciax_b200.synthetic import field_probabilities
 
-    model = build_model(local)
+    build_lib()
+    tp_parity = tp_preflight(rank, world, local) if world > 1 and not args.no_tp else None
+
+    # --- data parallel: every rank a full replica with its own batch ---
+    cfg = dict(CFG2, num_layers=args.layers)  # --layers: a shorter stack for profiling captures only
+    model = build_model(local, cfg=cfg)
     arrays = make_batch(seed=100 + rank)
-    tensors = {k: torch.from_numpy(np.ascontiguousarray(arrays[k]).astype(np.uint8 if arrays[k].dtype == bool else np.int32)).cuda()
-               for k in _lib.BATCH_KEYS}
+    tensors = device_batch(arrays)
     out = torch.empty(arrays["option_mask"].shape, dtype=torch.float32, device="cuda")
-    # A real stream: the library enqueues on it and the CUDA events below are
+    # A real stream: the library enqueues on it and the CUDA events are
     # recorded on it.  (torch's default stream is the legacy NULL stream, for
     # which the library would use its own stream instead.)
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
-
-    def barrier():
-        if dist:
-            dist.barrier()
-
-    # --- device-resident throughput ---
-    for _ in range(args.warmup):
-        model.forward_device(tensors, out, stream.cuda_stream)
-    torch.cuda.synchronize()
-    model.check_status()
-    barrier()
-    torch.cuda.synchronize()
-    model.set_timing(True)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            model.forward_device(tensors, out, stream.cuda_stream)
-        end.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    elapsed_ms = start.elapsed_time(end)
-    timing = model.timing_report()
-    model.set_timing(False)
-    model.check_status()
+    elapsed_ms, timing, clocks = timed_forwards(model, tensors, out, stream, args.steps, args.warmup, local, dist)
     launches = model.last_launch_count * args.steps
     logits_dev = out.cpu().numpy()
     if not np.isfinite(logits_dev[arrays["option_mask"]]).all():
         raise SystemExit("non-finite logits")
+
+    def barrier():
+        if dist:
+            dist.barrier()
 
     # --- end to end through the host API ---
     h2d = sum(int(np.asarray(arrays[k]).size * (1 if arrays[k].dtype == bool else 4)) for k in _lib.BATCH_KEYS)
@@ -362,6 +653,7 @@ def gpu_arm(args) -> None:
         logits = model.forward(arrays)
     e2e_s = time.perf_counter() - t0
     barrier()
+    model.close()
     decisions = sum(len(f) for f in field_probabilities(logits, arrays))
 
     elapsed_ms = rank_reduce(elapsed_ms, "max")
@@ -369,7 +661,7 @@ def gpu_arm(args) -> None:
     tokens = STATES * SEQ
     value = world * tokens * args.steps / (elapsed_ms / 1e3)
     e2e_value = world * tokens * args.steps / e2e_s
-    linear, attention, gu_flops_per_token = algorithmic_flops(CFG2, [SEQ] * STATES)
+    linear, attention, gu_flops_per_token = algorithmic_flops(cfg, [SEQ] * STATES)
     peaks = measured_peaks()
     step_s = elapsed_ms / 1e3 / args.steps
     gu_ms, gu_n = timing["gemm_gate_up"]
@@ -392,7 +684,7 @@ def gpu_arm(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (random-init weights, uniform token ids)",
-        "config": workload_config(world),
+        "config": workload_config(world) | ({"layers_override": args.layers} if args.layers != CFG2["num_layers"] else {}),
         "decisions_per_s": world * decisions * args.steps / (elapsed_ms / 1e3),
         "tensor_frac": {"flops_per_step": linear + attention, "achieved_tflops": (linear + attention) / step_s / 1e12,
                         "frac_of_measured_burst": (linear + attention) / step_s / 1e12 / peaks["bf16_tflops"],
@@ -407,15 +699,19 @@ def gpu_arm(args) -> None:
         "kernel_share": shares,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
-        "clocks": clocks.summary(),
+        "clocks": clocks,
     }
+    if world > 1 and not args.no_tp:
+        line["tp"] = tp_arm(args, rank, world, local, dist)
+        line["tp_parity"] = tp_parity
+    if world == 1 and not args.no_parity:
+        line["parity"] = cfg2_slice_parity(local)
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_sample(repeats=4)
         cb.pop("seconds", None)
         line["cpu_baseline"] = cb
     if rank == 0:
         print(json.dumps(line), flush=True)
-    model.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -920,6 +1216,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("cuda", "reference"), default="cuda")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="N=1: skip the cfg2-slice parity check against the oracle")
+    ap.add_argument("--no-tp", action="store_true", help="N>1: skip the TP=N preflight and timed run")
+    ap.add_argument("--layers", type=int, default=CFG2["num_layers"],
+                    help="cfg2 with fewer decoder layers: a small case for ncu captures of single kernels (not a bench line)")
     ap.add_argument("--serving-tp", action="store_true",
                     help="cfg5 under torchrun: one tensor-parallel model over the N GPUs instead of N replicas")
     ap.add_argument("--workload", choices=("cfg2", "cfg3", "cfg4", "cfg5", "attention", "attention4", "gdn", "rmsnorm"), default="cfg2",

@@ -102,6 +102,23 @@ class ClefEngine:
             raise ValueError("max_batch_tokens must be positive")
         self.max_batch_tokens = max_batch_tokens
         self._locks = [threading.Lock() for _ in self.replicas]
+        self._warm = False
+        self._warm_lock = threading.Lock()
+
+    def warmup(self) -> None:
+        """Reserve every replica's workspace for the largest batch this engine
+        forms (``ClefCudaModel.warmup``), so no request allocates device
+        memory.  ``decide_batch`` / ``decide_records`` call it once before
+        their first forward, so the reference server's warm-up request
+        (serve/app.py:385-406, one tiny ``decide``) reaches it."""
+        with self._warm_lock:
+            if self._warm:
+                return
+            for replica, lock in zip(self.replicas, self._locks):
+                if hasattr(replica, "warmup"):
+                    with lock:
+                        replica.warmup(max_batch_tokens=self.max_batch_tokens, max_rows=ROW_BUCKETS[-1])
+            self._warm = True
 
     def encode(self, states: Sequence[Any], questions: Mapping[Any, Mapping[str, Any]], max_len: int | None) -> list[Record]:
         model = self.model
@@ -121,6 +138,7 @@ class ClefEngine:
         forward, host arrays in and logits out)."""
         if not records:
             return []
+        self.warmup()
         batches = plan_batches([len(r.ids) for r in records], self.max_batch_tokens)
         results: list[dict[str, Any] | None] = [None] * len(records)
         work: queue.Queue[tuple[list[int], int]] = queue.Queue()

@@ -13,6 +13,7 @@ import ctypes
 import json
 import struct
 from collections.abc import Mapping, Sequence
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
 
@@ -20,8 +21,10 @@ import ml_dtypes
 import numpy as np
 
 from deciax_b200 import _lib
-from deciax_b200.clef_input import MAX_TOKENS, SEQUENCE_BUCKETS
+from deciax_b200.clef_input import (MAX_QUESTIONS, MAX_TOKENS, MAX_TOTAL_OPTIONS, ROW_BUCKETS, SCHEMA_BUCKETS,
+                                    SEQUENCE_BUCKETS, bucket)
 from deciax_b200.config import HeadConfig, KernelFlags, TextConfig
+from deciax_b200.engine import DEFAULT_BATCH_TOKENS
 
 INT_KEYS = ("input_ids", "lexical_ids", "lexical_spans", "question_spans", "types", "option_spans", "option_field")
 BOOL_KEYS = ("mask", "question_mask", "option_mask")
@@ -210,48 +213,21 @@ class ClefCudaModel:
     @classmethod
     def from_pretrained(cls, path: str | Path, dtype: str = "bf16", name: str = "clef", **kwargs: Any) -> "ClefCudaModel":
         """Load a Clef checkpoint directory (config.json, tokenizer.json,
-        model*.safetensors, joint_head_config.json, joint_head.safetensors) as
-        ``ClefModel.__init__`` does (models/clef/model.py:51-85, weights.py:70-101)."""
-        from tokenizers import Tokenizer
-
-        path = Path(path)
-        raw = json.loads((path / "config.json").read_text())
-        config = TextConfig.from_dict(raw)
-        if not config.vocab_size:
-            config = TextConfig(**{**config.__dict__, "vocab_size": int(raw.get("text_config", raw)["vocab_size"])})
-        tokenizer = Tokenizer.from_file(str(path / "tokenizer.json"))
-        pad_id = tokenizer.token_to_id("<|endoftext|>")
-        if pad_id is None:
-            raise ValueError("missing pad token")
-        head_cfg = json.loads((path / "joint_head_config.json").read_text())
-        head = dict(safetensors_tensors(path / "joint_head.safetensors"))
-        hc = HeadConfig(
-            heads=head_cfg["heads"],
-            routing_layers=head_cfg["routing_layers"],
-            layers=head_cfg["layers"],
-            width=int(head["memory_projection.weight"].shape[0]),
-            ffn=int(head["evidence_layers.0.feedforward.0.weight"].shape[0]) if head_cfg["routing_layers"] else int(head["layers.0.linear1.weight"].shape[0]),
-        )
-        m = cls(config, hc, dtype=dtype, name=name, tokenizer=tokenizer, pad_token_id=pad_id, **kwargs)
-        index = json.loads((path / "model.safetensors.index.json").read_text())["weight_map"]
-        for filename in sorted(set(index.values())):
-            for key, value in safetensors_tensors(path / filename):
-                if key.startswith("model.visual."):
-                    continue
-                if key == "lm_head.weight":
-                    m.upload("lm_head", value)
-                elif key == "model.language_model.embed_tokens.weight":
-                    m.upload("embedding", value)
-                elif key == "model.language_model.norm.weight":
-                    m.upload("norm", value)
-                elif key.startswith("model.language_model.layers."):
-                    _, _, _, number, rest = key.split(".", 4)
-                    rest = rest.replace("linear_attn.", "mixer.").replace("self_attn.", "mixer.")
-                    m.upload(f"layers.{number}.{rest}", value)
-                else:
-                    raise ValueError(f"unexpected backbone tensor: {key}")
-        for k, v in head.items():
-            m.upload("head." + k, v)
+        model*.safetensors with their index, joint_head_config.json,
+        joint_head.safetensors) as ``ClefModel.__init__`` does
+        (models/clef/model.py:51-85, weights.py:70-101).  The directory is
+        validated on the host first (``read_checkpoint``); the library then
+        keeps each tensor's tensor-parallel shard as it arrives, splitting the
+        Gated DeltaNet layers' fused ``in_proj_qkv`` / ``conv1d`` tensors."""
+        plan = read_checkpoint(path)
+        m = cls(plan.config, plan.head_config, dtype=dtype, name=name, tokenizer=plan.tokenizer,
+                pad_token_id=plan.pad_token_id, **kwargs)
+        for filename, names in plan.backbone.items():
+            for key, value in safetensors_tensors(filename):
+                if key in names:
+                    m.upload(names[key], value)
+        for key, value in safetensors_tensors(plan.head_file):
+            m.upload("head." + key, value)
         m.finalize()
         return m
 
@@ -319,6 +295,39 @@ class ClefCudaModel:
     def reserve(self, b: int, s: int, lx: int, o: int, q: int) -> None:
         _lib.check(self._lib.clef_reserve(self._handle, b, s, lx, o, q), self._handle)
 
+    def warmup(self, max_batch_tokens: int = DEFAULT_BATCH_TOKENS, max_rows: int = ROW_BUCKETS[-1],
+               max_options: int = MAX_TOTAL_OPTIONS, max_questions: int = MAX_QUESTIONS) -> None:
+        """Reserve the workspace for every batch a ``ClefEngine`` can form
+        under these limits, so that no later forward allocates (device
+        buffers, pinned staging, or -- under TP, where every rank must call
+        this with the same limits -- the exchange of peer-memory handles).
+
+        The engine's batches hold at most ``max_rows`` records padded to at
+        most ``max_token_budget`` tokens, with rows x padded length within
+        ``max_batch_tokens``; options and questions are bounded by the
+        protocol's limits (protocol/systemone.py:17,22).  Every workspace
+        term grows with one of rows x length, rows x options, rows x
+        questions or rows x lexical tokens (at most rows x length), so two
+        reservations cover them all: the longest records at the most rows
+        the token budget allows, and the most rows at the length the budget
+        then allows.  The reference server's warm-up request
+        (serve/app.py:385-406) compiles one small shape; this reserves the
+        whole admitted range."""
+        s_max = self.max_token_budget
+        o = bucket(max_options, SCHEMA_BUCKETS)
+        q = bucket(max_questions, SCHEMA_BUCKETS)
+        long_rows = max(1, min(max_rows, max_batch_tokens // s_max))
+        many_seq = max(1, min(s_max, max_batch_tokens // max_rows))
+        for b, s in ((long_rows, s_max), (max_rows, many_seq)):
+            self.reserve(b, s, bucket(s, SEQUENCE_BUCKETS), o, q)
+
+    @property
+    def workspace_allocations(self) -> int:
+        """Workspace growths since creation (see ``clef_workspace_allocations``)."""
+        n = ctypes.c_int64()
+        _lib.check(self._lib.clef_workspace_allocations(self._handle, ctypes.byref(n)), self._handle)
+        return int(n.value)
+
     def check_status(self) -> None:
         _lib.check(self._lib.clef_check_status(self._handle), self._handle)
 
@@ -343,21 +352,138 @@ class ClefCudaModel:
             pass
 
 
+SAFETENSORS_TYPES = {"BF16": ml_dtypes.bfloat16, "F32": np.float32, "F16": np.float16}
+
+
+def safetensors_header(path: Path) -> tuple[int, dict[str, Any]]:
+    """(header length, {name: {dtype, shape, data_offsets}}) of a safetensors
+    file, checked the way the reference has ``safe_open`` check it before
+    mapping (weights.py:26-31): a supported dtype, offsets inside the data
+    section and a byte size that matches the shape."""
+    path = Path(path)
+    total = path.stat().st_size
+    with open(path, "rb") as f:
+        raw = f.read(8)
+        if len(raw) != 8:
+            raise ValueError(f"{path.name}: not a safetensors file")
+        size = struct.unpack("<Q", raw)[0]
+        if 8 + size > total:
+            raise ValueError(f"{path.name}: header runs past the end of the file")
+        try:
+            header = json.loads(f.read(size))
+        except json.JSONDecodeError as e:
+            raise ValueError(f"{path.name}: unreadable header ({e})") from None
+    data = total - 8 - size
+    for key, entry in header.items():
+        if key == "__metadata__":
+            continue
+        if entry.get("dtype") not in SAFETENSORS_TYPES:
+            raise ValueError(f"{path.name}: {key} has unsupported dtype {entry.get('dtype')!r}")
+        start, end = entry["data_offsets"]
+        nbytes = int(np.prod(entry["shape"], dtype=np.int64)) * np.dtype(SAFETENSORS_TYPES[entry["dtype"]]).itemsize
+        if not 0 <= start <= end <= data or end - start != nbytes:
+            raise ValueError(f"{path.name}: {key} has invalid data offsets")
+    return size, header
+
+
 def safetensors_tensors(path: Path):
-    """Yield (name, array) from a safetensors file via memmap; BF16 as ml_dtypes.
+    """Yield (name, array) from a safetensors file via memmap; BF16 as ml_dtypes
+    (models/clef/weights.py:26-40).
 
     The file format is an 8-byte little-endian header length, a JSON header
     of {name: {dtype, shape, data_offsets}}, then the raw data.
     """
-    with open(path, "rb") as f:
-        size = struct.unpack("<Q", f.read(8))[0]
-        header = json.loads(f.read(size))
-    types = {"BF16": ml_dtypes.bfloat16, "F32": np.float32, "F16": np.float16}
+    size, header = safetensors_header(path)
     for key, entry in header.items():
         if key == "__metadata__":
             continue
-        start, end = entry["data_offsets"]
-        arr = np.memmap(path, mode="r", dtype=types[entry["dtype"]], offset=8 + size + start, shape=tuple(entry["shape"]))
+        start, _ = entry["data_offsets"]
+        arr = np.memmap(path, mode="r", dtype=SAFETENSORS_TYPES[entry["dtype"]], offset=8 + size + start,
+                        shape=tuple(entry["shape"]))
         if entry["dtype"] == "F16":
             arr = np.asarray(arr, np.float32)
         yield key, arr
+
+
+@dataclass(frozen=True)
+class CheckpointPlan:
+    """What ``from_pretrained`` will load, read from headers only."""
+
+    config: TextConfig
+    head_config: HeadConfig
+    tokenizer: Any
+    pad_token_id: int
+    backbone: dict[Path, dict[str, str]]  # shard file -> {checkpoint key: library upload name}
+    head_file: Path
+
+
+def backbone_name(key: str, num_layers: int) -> str | None:
+    """The library's upload name for a backbone checkpoint key, or None for a
+    key the reference skips (the vision tower); the renames of
+    models/clef/weights.py:43-45,84-93.  Gated DeltaNet layers keep their
+    fused ``in_proj_qkv`` / ``conv1d`` names: the library splits them into the
+    q, k, v parts of weights.py:46-55 as it shards."""
+    if key.startswith("model.visual."):
+        return None
+    if key == "lm_head.weight":
+        return "lm_head"
+    if key == "model.language_model.embed_tokens.weight":
+        return "embedding"
+    if key == "model.language_model.norm.weight":
+        return "norm"
+    if key.startswith("model.language_model.layers."):
+        parts = key.split(".", 4)
+        if len(parts) == 5 and parts[3].isdigit() and int(parts[3]) < num_layers:
+            rest = parts[4].replace("linear_attn.", "mixer.").replace("self_attn.", "mixer.")
+            return f"layers.{int(parts[3])}.{rest}"
+    raise ValueError(f"unexpected backbone tensor: {key}")
+
+
+def read_checkpoint(path: str | Path) -> CheckpointPlan:
+    """Validate a Clef checkpoint directory on the host, before any device
+    work, with the reference's rejections (models/clef/model.py:51-57,
+    weights.py:70-101): the ``config.json`` checks of ``TextConfig.from_dict``,
+    a tokenizer without ``<|endoftext|>`` ("missing pad token"), an unexpected
+    backbone key, and a text checkpoint without its embedding, lm_head, final
+    norm or any tensor of some layer ("incomplete Clef text checkpoint")."""
+    from tokenizers import Tokenizer
+
+    path = Path(path)
+    raw = json.loads((path / "config.json").read_text())
+    config = TextConfig.from_dict(raw)
+    if not config.vocab_size:
+        config = TextConfig(**{**config.__dict__, "vocab_size": int(raw.get("text_config", raw)["vocab_size"])})
+    tokenizer = Tokenizer.from_file(str(path / "tokenizer.json"))
+    pad_id = tokenizer.token_to_id("<|endoftext|>")
+    if pad_id is None:
+        raise ValueError("missing pad token")
+    n = len(config.layer_types)
+    index = json.loads((path / "model.safetensors.index.json").read_text())["weight_map"]
+    backbone: dict[Path, dict[str, str]] = {}
+    top, layers = set(), [0] * n
+    for filename in sorted(set(index.values())):
+        names = backbone.setdefault(path / filename, {})
+        for key in safetensors_header(path / filename)[1]:
+            if key == "__metadata__":
+                continue
+            upload = backbone_name(key, n)
+            if upload is None:
+                continue
+            names[key] = upload
+            if upload.startswith("layers."):
+                layers[int(upload.split(".")[1])] += 1
+            else:
+                top.add(upload)
+    if top != {"lm_head", "embedding", "norm"} or not all(layers):
+        raise ValueError("incomplete Clef text checkpoint")
+    head_cfg = json.loads((path / "joint_head_config.json").read_text())
+    head_file = path / "joint_head.safetensors"
+    shapes = {k: v["shape"] for k, v in safetensors_header(head_file)[1].items() if k != "__metadata__"}
+    if "memory_projection.weight" not in shapes:
+        raise ValueError("missing joint head tensor: memory_projection.weight")
+    ffn_key = "evidence_layers.0.feedforward.0.weight" if head_cfg["routing_layers"] else "layers.0.linear1.weight"
+    if ffn_key not in shapes:
+        raise ValueError(f"missing joint head tensor: {ffn_key}")
+    hc = HeadConfig(heads=head_cfg["heads"], routing_layers=head_cfg["routing_layers"], layers=head_cfg["layers"],
+                    width=int(shapes["memory_projection.weight"][0]), ffn=int(shapes[ffn_key][0]))
+    return CheckpointPlan(config, hc, tokenizer, pad_id, backbone, head_file)

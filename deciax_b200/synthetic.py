@@ -165,8 +165,11 @@ def _head_weights(rng, D: int, head: HeadConfig, std: float, cast):
     hp["residual_scorer.0.bias"] = n(W)
     hp["residual_scorer.3.weight"] = n(1, W, s=W**-0.5)
     hp["residual_scorer.3.bias"] = n(1)
-    hp["prior_logit_scale"] = cast(np.array(np.log(10.0), np.float32))
-    hp["joint_logit_scale"] = cast(np.array(np.log(10.0), np.float32))
+    # The head module's own initial values, as the reference's head fixture
+    # holds them (tests/fixtures/clef_head.npz: all three 0, i.e. logit
+    # scales exp(0) = 1 and a residual gate of sigmoid(0)).
+    hp["prior_logit_scale"] = cast(np.array(0.0, np.float32))
+    hp["joint_logit_scale"] = cast(np.array(0.0, np.float32))
     hp["residual_gate"] = cast(np.array(0.0, np.float32))
     return hp
 

@@ -89,3 +89,28 @@ def test_engine_data_parallel_over_gpus():
     got = ClefEngine(replicas[0], replicas=replicas, max_batch_tokens=4096).decide_batch(ss, questions)
     want = one_by_one(replicas[0], ss, questions)
     compare(got, want, 1e-4)
+
+
+def test_requests_after_warmup_allocate_nothing():
+    """The engine's warm-up (reached by the first ``decide_batch``, as the
+    reference server's warm-up request reaches ``decide``,
+    serve/app.py:385-406) reserves the workspace for every batch the engine
+    can form, so later requests of any length and schema allocate no device
+    memory, no pinned staging and exchange no handles."""
+    model = replica(0, "bf16")
+    engine = ClefEngine(model, max_batch_tokens=4096)
+    engine.decide_batch(["warmup"], {"q": {"type": "noul", "instructions": "Is this a warmup request?"}})
+    after_warmup = model.workspace_allocations
+    assert after_warmup > 0
+    for name in ("mixed", "reference_test"):
+        questions = FIX["schemas"][name]
+        engine.decide_batch(states(30), questions)  # long and short states, several batch shapes
+        engine.decide_batch(FIX["states"][:1], questions)
+    assert model.workspace_allocations == after_warmup
+    # without the warm-up a larger batch than any before grows the workspace
+    cold = replica(0, "bf16")
+    r = I.encode(TOK, states(1)[0], FIX["schemas"]["mixed"], cold.max_token_budget)
+    cold.forward(I.collate([r], PAD))
+    first = cold.workspace_allocations
+    cold.forward(I.collate([r] * 4, PAD))
+    assert cold.workspace_allocations > first
