@@ -36,7 +36,6 @@
 #include "../../include/clef_b200.h"
 #include "attention.cuh"
 #include "attention_sm100.cuh"
-#include "attention_pair_sm100.cuh"
 #include "common.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm2_sm100.cuh"
@@ -526,29 +525,7 @@ static void attention(Launcher& L, const AttnArgs<T>& a) {
       } else if (a.hd == 128) {
         launch(attn_tc_kernel<128>, AttnTcShape<128>::SMEM, 128);
       } else {
-        // head_dim 256: CTA pairs over 256 query rows and 128-key tiles
-        auto kern = attn_pair_kernel<256>;
-        constexpr size_t smem = AttnPairShape<256>::SMEM;
-        {
-          std::lock_guard<std::mutex> lock(mu_tc);
-          if (!done_tc.count({dev, -256})) {
-            CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-            done_tc.insert({dev, -256});
-          }
-        }
-        cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3(2 * ((a.Lq + 255) / 256), a.H, a.B);
-        cfg.blockDim = dim3(AttnPairShape<256>::THREADS);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = L.stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, map, out_map, t));
+        launch(attn_tc_kernel<256>, AttnTcShape<256>::SMEM, 256);
       }
       done = true;
     }

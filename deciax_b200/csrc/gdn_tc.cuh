@@ -155,12 +155,24 @@ __device__ __forceinline__ void gdn_tc_load_chunk(const GdnArgs& a, const __nv_b
     if constexpr (NK == 1) load_kind(kind, raw[0]);
     const uint4 (&rk)[NX] = raw[NK == 3 ? kind : 0];
     float w[VN][W];
-#pragma unroll
-    for (int c = 0; c < VN; ++c)
+    if (wsm) {  // taps staged [kind][tap][channel]: 16-byte reads of 4 channels, no bank conflicts
 #pragma unroll
       for (int i = 0; i < W; ++i)
-        w[c][i] = wsm ? wsm[(kind * DH + g * VN + c) * W + i]
-                      : (i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f);
+#pragma unroll
+        for (int c = 0; c < VN; c += 4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(wsm + (kind * W + i) * DH + g * VN + c);
+          w[c][i] = t4.x;
+          w[c + 1][i] = t4.y;
+          w[c + 2][i] = t4.z;
+          w[c + 3][i] = t4.w;
+        }
+    } else {
+#pragma unroll
+      for (int c = 0; c < VN; ++c)
+#pragma unroll
+        for (int i = 0; i < W; ++i)
+          w[c][i] = i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f;
+    }
     float x[NX][VN];
 #pragma unroll
     for (int i = 0; i < NX; ++i) {
@@ -223,7 +235,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   float* bs = gs + C;                                      // beta
   float* es = bs + C;                                      // e^g
   float* ws = es + C;                                      // e^(g_last - g)
-  float* wconv = ws + C;                                   // [3][DH][4] conv taps (width <= 4)
+  float* wconv = ws + C;                                   // [3][4][DH] conv taps (width <= 4)
   float* red = wconv + 3 * DH * 4;                         // [2][C] output-row partial sums of squares
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(red + 2 * C);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
@@ -256,8 +268,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
   if (a.width <= 4) {
     const int shift = 4 - a.width;
-    for (int i = tid; i < 3 * DH * 4; i += kGdnThreads) {
-      const int kind = i / (DH * 4), c = (i / 4) % DH, tap = i % 4;
+    for (int i = tid; i < 3 * DH * 4; i += kGdnThreads) {  // [kind][tap][channel]
+      const int kind = i / (DH * 4), tap = (i / DH) % 4, c = i % DH;
       const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + c;
       wconv[i] = tap >= shift ? to_f32(convw[static_cast<long long>(col) * a.width + (tap - shift)]) : 0.f;
     }
@@ -280,21 +292,22 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   const int chunks = (a.S + C - 1) / C;
   for (int ci = 0; ci < chunks; ++ci) {
     const int t0 = ci * C;
-    // ---- L: conv + SiLU, L2 norms, gates ----
+    // ---- L: conv + SiLU, L2 norms, gates (the gate inputs are loaded first,
+    // so their latency overlaps the convolution) ----
+    float ga = 0.f, gb = 0.f;
+    const bool gate_row = tid < C && t0 + tid < a.S;
+    if (gate_row) {
+      const T* pr = proj + (row0 + t0 + tid) * a.ldp;
+      ga = to_f32(pr[a.a_col + h]);
+      gb = to_f32(pr[a.b_col + h]);
+    }
     if (a.width <= 4)
       gdn_tc_load_chunk<4>(a, proj, convw, wconv, row0, t0, q_col, k_col, v_col, sA0, sV);
     else
       gdn_tc_load_chunk<8>(a, proj, convw, nullptr, row0, t0, q_col, k_col, v_col, sA0, sV);
     if (tid < C) {
-      const int t = t0 + tid;
-      if (t < a.S) {
-        const T* pr = proj + (row0 + t) * a.ldp;
-        gs[tid] = neg_a * softplus_f(to_f32(pr[a.a_col + h]) + dt_bias);
-        bs[tid] = round_to<T>(sigmoid_fast(to_f32(pr[a.b_col + h])));
-      } else {
-        gs[tid] = 0.f;
-        bs[tid] = 0.f;
-      }
+      gs[tid] = gate_row ? neg_a * softplus_f(ga + dt_bias) : 0.f;
+      bs[tid] = gate_row ? round_to<T>(sigmoid_fast(gb)) : 0.f;
     }
     fence_async_smem();
     __syncthreads();
@@ -375,19 +388,21 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
 #pragma unroll
       for (int r = 0; r < C; ++r) {
         float* p = reinterpret_cast<float*>(vcol ? sV + gdn_sw_mn(r, col, C) : sA0 + gdn_sw(r, col, 2 * C));
-        float acc = vcol ? *p * bs[r] : *p * bs[r] * es[r];
+        // four independent partial sums (stride-4 terms): the row's latency is
+        // r/4 dependent FMAs instead of r
+        float acc[4] = {vcol ? *p * bs[r] : *p * bs[r] * es[r], 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j4 = 0; j4 + 4 <= r; j4 += 4) {
           const float4 a4 = *reinterpret_cast<const float4*>(As + r * LDA + j4);
-          acc = fmaf(a4.x, x[j4], acc);
-          acc = fmaf(a4.y, x[j4 + 1], acc);
-          acc = fmaf(a4.z, x[j4 + 2], acc);
-          acc = fmaf(a4.w, x[j4 + 3], acc);
+          acc[0] = fmaf(a4.x, x[j4], acc[0]);
+          acc[1] = fmaf(a4.y, x[j4 + 1], acc[1]);
+          acc[2] = fmaf(a4.z, x[j4 + 2], acc[2]);
+          acc[3] = fmaf(a4.w, x[j4 + 3], acc[3]);
         }
 #pragma unroll
-        for (int j = r & ~3; j < r; ++j) acc = fmaf(As[r * LDA + j], x[j], acc);
-        x[r] = acc;
-        *p = vcol ? acc : to_tf32(acc);  // U stays FP32; W becomes an operand
+        for (int j = r & ~3; j < r; ++j) acc[j & 3] = fmaf(As[r * LDA + j], x[j], acc[j & 3]);
+        x[r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        *p = vcol ? x[r] : to_tf32(x[r]);  // U stays FP32; W becomes an operand
       }
     }
     fence_async_smem();
@@ -474,10 +489,10 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[32 * part + e] = round_to<T>(__uint_as_float(d[e]));
       }
-      float ss = 0.f;
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < 64; ++e) ss += o[e] * o[e];
-      red[half * C + c] = ss;
+      for (int e = 0; e < 64; ++e) sq[e & 3] = fmaf(o[e], o[e], sq[e & 3]);
+      red[half * C + c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
       asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 2, 3, 6, 7
       const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
       if (t < a.S) {

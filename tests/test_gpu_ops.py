@@ -275,10 +275,9 @@ def test_attention_bf16_flash(d, s):
 
 @pytest.mark.parametrize("d", [128, 256])
 def test_attention_bf16_long_rows_with_rescales(d):
-    """Many key tiles per query tile, scores large enough that the running
-    max moves by more than the lazy-rescale margin (head_dim 128: one CTA,
-    64-key tiles; 256: CTA pairs, 128-key tiles; both keep P in tensor
-    memory)."""
+    """Many 64-key tiles per query tile, scores large enough that the running
+    max moves by more than the lazy-rescale margin (head_dim 128 keeps P in
+    tensor memory; 256 in shared memory)."""
     got, expected = attention_case("bf16", d, 1024, lengths=[1024, 700], qscale=6.0, seed=3)
     np.testing.assert_allclose(got, expected, rtol=2e-2, atol=2e-2)
     assert np.abs(got - expected).mean() < 2e-3
@@ -291,11 +290,9 @@ def test_attention_fp32_exact(d):
 
 
 @pytest.mark.parametrize("s,lengths", [(384, [384, 300]), (2048, [2048, 1999])])
-def test_attention_bf16_d256_pair_tiles(s, lengths):
-    """head_dim 256 runs on CTA pairs over 256 query rows: a sequence of 384
-    leaves the second CTA of the last pair past the end (it must store
-    nothing) while every 128-row tile leaves through TMA stores; 2048 is the
-    benchmark layer's length."""
+def test_attention_bf16_d256_long_sequences(s, lengths):
+    """head_dim 256 at 384 tokens (three 128-row tiles, each leaving through
+    TMA stores) and at the benchmark layer's 2048, with a ragged second row."""
     got, expected = attention_case("bf16", 256, s, lengths=lengths, seed=5)
     np.testing.assert_allclose(got, expected, rtol=2e-2, atol=2e-2)
     assert np.abs(got - expected).mean() < 2e-3
