@@ -4,38 +4,39 @@
 //
 // One CTA per (state, value head) walks the sequence in 64-token chunks.  The
 // FP32 state S [dk, dv] stays in shared memory in the layout of a tcgen05
-// B operand.  Per chunk (c, c' tokens; i key dims; j value dims):
+// B operand.  Per chunk (c, c' tokens of the chunk):
 //   L  conv + SiLU, L2 norms and gates as the CUDA-core kernel (gdn.cuh),
 //      written straight into operand layouts: A0 = [k; q] (128 rows), v.
-//   M0 D0 = A0 k^T (tcgen05, M = 128, N = 64, K = 128): rows 0-63 k k^T,
-//      rows 64-127 q k^T.
-//   P  rows 0-63 -> the strictly lower system A = -(k beta k^T) * decay;
+//   M0 D0 = A0 k^T (M = 128, N = 64, K = 128): rows 0-63 k k^T, rows 64-127 q k^T.
+//   M1 D1 = A0 S (N = 128): rows 0-63 k S, rows 64-127 q S.
+//   P  rows 0-63 of D0 -> the strictly lower system A = -(k beta k^T) * decay;
 //      rows 64-127 -> M = (q k^T) * decay (c' <= c), written back into tensor
-//      memory as the A operand of M2; q -> q e^g in place; K~^T = (k e^{g_C - g})^T
-//      into tensor memory (the A operand of M3).
-//   T  exact forward substitution (I - A) X = [v beta | k beta e^g] on the
-//      CUDA cores, one right-hand column per thread, in place: U = X_v
-//      (reference.py:81 `value`), W = X_k (`cumulative_key`), so A0 = [W; q e^g].
-//   M1 D1 = A0 S (M = 128, N = 128, K = 128): rows 0-63 W S, rows 64-127 (q e^g) S.
-//   V  V_new = U - W S (reference.py:83), in place of U.
-//   M2 D1 += [. ; M] V_new (K = 64): rows 64-127 become the chunk's output
-//      (q e^g) S + (q k^T * decay) V_new (reference.py:85).
-//   M3 D2 = K~^T V_new (M = 128, N = 128, K = 64), then S = S e^{g_C} + D2
+//      memory as the A operand of M3; K~^T = (k e^{g_C - g})^T into tensor
+//      memory (the A operand of M4); R = v - e^g * (k S) in place of v.
+//   T  the inverse T = (I - A)^{-1} (reference.py:73-80) by exact forward
+//      substitution on the CUDA cores, one column per thread, stored as
+//      T diag(beta).
+//   MV V_new = T diag(beta) R (K = 64).  This is reference.py:81-83's
+//      T (v beta) - T (k beta e^g) S, regrouped so that neither product with
+//      T runs over the value and the key dims separately.
+//   M3 D3 = M V_new (A from tensor memory, K = 64).
+//   M4 D2 = K~^T V_new (M = 128, N = 128, K = 64); S = S e^{g_C} + D2
 //      (reference.py:86).
-//   O  gated RMSNorm x SiLU(z) of the output rows (text.py:61-67).
+//   O  rows c: e^{g_c} (q S)_c + D3_c (reference.py:85), then the gated
+//      RMSNorm x SiLU(z) (text.py:61-67).
 // Products run as kind::tf32 (operands rounded to TF32, FP32 accumulation);
-// the solve, the gates and every elementwise step are FP32.  The FP32 parity
-// mode keeps the all-FP32 CUDA-core kernel.
+// the inverse, the gates and every elementwise step are FP32.  The FP32
+// parity mode keeps the all-FP32 CUDA-core kernel.
 //
-// Layouts: every operand is rows of 32 fp32 (128 B) in atoms of `rows` rows
-// per 32 columns: a K-major operand stores [M or N rows][K] with the 128-byte
-// swizzle (16-byte chunks XOR row % 8), an MN-major one [K rows][M or N] with
-// the 128-byte swizzle of 32-byte atomicity (32-byte chunks XOR row % 4), the
-// only swizzle tcgen05 takes for 32-bit MN-major operands.
-// Tensor memory (512 columns): D0 [0, 64), D1 [64, 192), D2 [192, 320),
-// K~^T [320, 384).  One thread issues the MMAs and commits to one mbarrier;
-// every wait is bounded.  Rows past the sequence end are zero with g = beta
-// = 0, as the reference's padding.
+// Operand tiles are rows of 32 fp32 (128 B) in atoms of `rows` rows per 32
+// columns: a K-major operand [M or N rows][K] with the 128-byte swizzle
+// (16-byte chunks XOR row % 8), an MN-major one [K rows][M or N] with the
+// 128-byte swizzle of 32-byte atomicity (32-byte chunks XOR row % 4), the only
+// swizzle tcgen05 takes for 32-bit MN-major operands.  Tensor memory (512
+// columns): D0 [0, 64), D1 [64, 192), V_new product then D3 [192, 320), D2
+// [320, 448), K~^T [448, 512).  One thread issues the MMAs and commits to one
+// mbarrier; every wait is bounded.  Rows past the sequence end are zero with
+// g = beta = 0, as the reference's padding.
 #pragma once
 
 #include "attention_sm100.cuh"
@@ -49,12 +50,13 @@ constexpr int kGdnTcDim = 128;
 struct GdnTcShape {
   static constexpr int C = kGdnChunk, DH = kGdnTcDim, LDA = C + 4;
   static constexpr uint32_t S_BYTES = DH * DH * 4;        // state, MN-major B [dk rows][dv]
-  static constexpr uint32_t A0_BYTES = 2 * C * DH * 4;    // [k; q] then [W; q e^g], K-major [128 rows][dk]
-  static constexpr uint32_t V_BYTES = C * DH * 4;         // v beta -> U -> V_new, MN-major [tokens][dv]
+  static constexpr uint32_t A0_BYTES = 2 * C * DH * 4;    // [k; q], K-major [128 rows][dk]
+  static constexpr uint32_t V_BYTES = C * DH * 4;         // v -> R -> V_new, MN-major [tokens][dv]
+  static constexpr uint32_t T_BYTES = 2 * C * C * 4;      // T diag(beta), K-major [128 rows][64]; rows 64-127 zero
   static constexpr uint32_t AS_BYTES = C * LDA * 4;       // system matrix, row-major
-  static constexpr uint32_t MISC_FLOATS = 4 * C + 3 * DH * 4 + 2 * C;  // gates, conv taps, norm partial sums
-  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + AS_BYTES + MISC_FLOATS * 4 + 64;
-  static constexpr uint32_t D0 = 0, D1 = 64, D2 = 192, KT = 320, TMEM_COLS = 512;
+  static constexpr uint32_t MISC_FLOATS = 4 * C + 3 * DH * 4 + 2 * C + 32 * 33;  // gates, conv taps, norm partial sums, inverse blocks
+  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + AS_BYTES + MISC_FLOATS * 4 + 64;
+  static constexpr uint32_t D0 = 0, D1 = 64, DV = 192, D2 = 320, KT = 448, TMEM_COLS = 512;
 };
 
 // Byte offset of element (row, col) of a K-major fp32 operand tile (rows =
@@ -221,25 +223,25 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   using Sh = GdnTcShape;
   using T = __nv_bfloat16;
   constexpr int C = Sh::C, DH = Sh::DH, LDA = Sh::LDA;
-  constexpr uint32_t IDESC_G = idesc_tf32_f32(128, C, false, false);     // A0 k^T: both K-major
-  constexpr uint32_t IDESC_S = idesc_tf32_f32(128, DH, false, true);     // A0 S: S is MN-major
-  constexpr uint32_t IDESC_V = idesc_tf32_f32(128, DH, false, true);     // (tmem A) V_new: V_new is MN-major
+  constexpr uint32_t IDESC_G = idesc_tf32_f32(128, C, false, false);  // A0 k^T: both K-major
+  constexpr uint32_t IDESC_N = idesc_tf32_f32(128, DH, false, true);  // x S, T R, (tmem A) V_new: B MN-major
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sS = smem;
   uint8_t* sA0 = sS + Sh::S_BYTES;
   uint8_t* sV = sA0 + Sh::A0_BYTES;
-  float* As = reinterpret_cast<float*>(sV + Sh::V_BYTES);  // [C][LDA]
+  uint8_t* sT = sV + Sh::V_BYTES;
+  float* As = reinterpret_cast<float*>(sT + Sh::T_BYTES);  // [C][LDA]
   float* gs = As + C * LDA;                                // cumulative g
   float* bs = gs + C;                                      // beta
   float* es = bs + C;                                      // e^g
   float* ws = es + C;                                      // e^(g_last - g)
   float* wconv = ws + C;                                   // [3][4][DH] conv taps (width <= 4)
   float* red = wconv + 3 * DH * 4;                         // [2][C] output-row partial sums of squares
-  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(red + 2 * C);
+  float* yb = red + 2 * C;                                 // [32][33] products of the blocked inverse
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(yb + 32 * 33);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
-  int* fail = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -258,7 +260,6 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
 
   if (tid == 0) {
     mbar_init(mma_bar, 1);
-    *fail = 0;
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -266,6 +267,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     tmem_relinquish();
   }
   for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
+  // rows 64-127 of the T operand stay zero: the MV product's lanes 64-127 are unused
+  for (int i = tid; i < 2 * C * C; i += kGdnThreads) reinterpret_cast<float*>(sT)[i] = 0.f;
   if (a.width <= 4) {
     const int shift = 4 - a.width;
     for (int i = tid; i < 3 * DH * 4; i += kGdnThreads) {  // [kind][tap][channel]
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     return __syncthreads_and(ok) != 0;
   };
 
-  const uint32_t a0 = smem_u32(sA0), sv = smem_u32(sV), ss_addr = smem_u32(sS);
+  const uint32_t a0 = smem_u32(sA0), sv = smem_u32(sV), st = smem_u32(sT), ss_addr = smem_u32(sS);
   const int chunks = (a.S + C - 1) / C;
   for (int ci = 0; ci < chunks; ++ci) {
     const int t0 = ci * C;
@@ -311,7 +314,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     }
     fence_async_smem();
     __syncthreads();
-    // cumulative gate (sequential, as cumsum) and its exponentials; M0 meanwhile
+    // cumulative gate (sequential, as cumsum) and its exponentials; M0 and M1 meanwhile
     if (warp == 0) {
       if (lane == 0) {
         float acc = 0.f;
@@ -328,17 +331,20 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       }
     }
     if (tid == 32) {
-      // ---- M0: D0 = [k; q] k^T (the k operand values are exact in TF32: bf16 after the norm) ----
+      // ---- M0: D0 = [k; q] k^T;  M1: D1 = [k; q] S (the k operand values
+      // are exact in TF32: bf16 after the norm) ----
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < DH / 8; ++kk) {
         const uint32_t off = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
         umma_tf32(tmem + Sh::D0, smem_desc_k128(a0 + off), smem_desc_k128(a0 + off), IDESC_G, kk > 0 ? 1u : 0u);
+        umma_tf32(tmem + Sh::D1, smem_desc_k128(a0 + off), smem_desc_mn128_32b(ss_addr + kk * 1024, DH * 128),
+                  IDESC_N, kk > 0 ? 1u : 0u);
       }
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
-    // ---- P: system matrix, M, q e^g, K~^T ----
+    // ---- P: system matrix (lanes 0-63) or M (lanes 64-127); K~^T; R (lanes 0-63) ----
     {
       // this thread: tensor-memory lane lrow, D0 columns [32 half, +32)
       uint32_t d[32];
@@ -362,101 +368,164 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
         }
         tmem_st32(tmem + t_lane + Sh::D0 + 32 * half, d);
       }
-      // K~^T: lane i (key dim) x columns c in [32 half, +32): k[c][i] e^{g_last - g_c}
-      uint32_t kt[32];
+      // K~^T: lane (key dim) x columns c in [32 half, +32): k[c][key] e^{g_last - g_c}
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int c = 32 * half + e;
-        kt[e] = __float_as_uint(to_tf32(*reinterpret_cast<const float*>(sA0 + gdn_sw(c, lrow, 2 * C)) * ws[c]));
+        d[e] = __float_as_uint(to_tf32(*reinterpret_cast<const float*>(sA0 + gdn_sw(c, lrow, 2 * C)) * ws[c]));
       }
-      tmem_st32(tmem + t_lane + Sh::KT + 32 * half, kt);
+      tmem_st32(tmem + t_lane + Sh::KT + 32 * half, d);
+      if (lrow < C) {
+        // R = v - e^g (k S), value dims [64 half, +64)
+        const int c = lrow;
+        const float ec = es[c];
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int j0 = 64 * half + 32 * part;
+          tmem_ld32(tmem + t_lane + Sh::D1 + j0, d);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4* p = reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e, C));
+            float4 u = *p;
+            u.x = to_tf32(fmaf(-ec, __uint_as_float(d[e]), u.x));
+            u.y = to_tf32(fmaf(-ec, __uint_as_float(d[e + 1]), u.y));
+            u.z = to_tf32(fmaf(-ec, __uint_as_float(d[e + 2]), u.z));
+            u.w = to_tf32(fmaf(-ec, __uint_as_float(d[e + 3]), u.w));
+            *p = u;
+          }
+        }
+      }
       tmem_wait_st();
-      // q -> q e^g (rows 64-127 of A0), rounded to TF32
-      for (int idx = tid; idx < C * DH; idx += kGdnThreads) {
-        const int r = idx / DH, col = idx % DH;
-        float* p = reinterpret_cast<float*>(sA0 + gdn_sw(C + r, col, 2 * C));
-        *p = to_tf32(*p * es[r]);
-      }
     }
-    tc_fence_before();
     __syncthreads();
-    // ---- T: (I - A) X = [v beta | k beta e^g], one column per thread, in place ----
+    // ---- T: (I - A)^{-1} by blocks, in the T operand tile (rows 0-63), then
+    // scaled by beta per column and rounded to TF32.  Diagonal 16 x 16 blocks by
+    // forward substitution; then for [[P, 0], [Q, R]] with known inverses P', R'
+    // the lower-left block of the inverse is R' (Q~ P'), Q~ = the system
+    // entries (A holds minus the matrix's off-diagonal), first for the 16 x 16
+    // pairs of blocks, then for the two 32 x 32 halves ----
     {
-      const bool vcol = tid < DH;
-      const int col = vcol ? tid : tid - DH;
-      float x[C];
+      auto tf = [&](int r, int c) -> float& { return *reinterpret_cast<float*>(sT + gdn_sw(r, c, 2 * C)); };
+      if (tid < C) {
+        const int b0 = (tid >> 4) * 16, c = tid & 15;
+        float x[16];
 #pragma unroll
-      for (int r = 0; r < C; ++r) {
-        float* p = reinterpret_cast<float*>(vcol ? sV + gdn_sw_mn(r, col, C) : sA0 + gdn_sw(r, col, 2 * C));
-        // four independent partial sums (stride-4 terms): the row's latency is
-        // r/4 dependent FMAs instead of r
-        float acc[4] = {vcol ? *p * bs[r] : *p * bs[r] * es[r], 0.f, 0.f, 0.f};
+        for (int r = 0; r < 16; ++r) {
+          const float* arow = As + (b0 + r) * LDA + b0;
+          float acc0 = r == c ? 1.f : 0.f, acc1 = 0.f;
 #pragma unroll
-        for (int j4 = 0; j4 + 4 <= r; j4 += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(As + r * LDA + j4);
-          acc[0] = fmaf(a4.x, x[j4], acc[0]);
-          acc[1] = fmaf(a4.y, x[j4 + 1], acc[1]);
-          acc[2] = fmaf(a4.z, x[j4 + 2], acc[2]);
-          acc[3] = fmaf(a4.w, x[j4 + 3], acc[3]);
+          for (int j = 0; j < r; ++j) {
+            if (j & 1)
+              acc1 = fmaf(arow[j], x[j], acc1);
+            else
+              acc0 = fmaf(arow[j], x[j], acc0);
+          }
+          x[r] = acc0 + acc1;
+          tf(b0 + r, b0 + c) = x[r];
+        }
+      }
+      __syncthreads();
+      // pairs of 16-blocks: Y = A[B0 + r][A0 + k] T[A0 + k][A0 + c]  (T's upper parts are zero)
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
+        const float* arow = As + (b0b + r) * LDA + a0b;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = fmaf(arow[k], tf(a0b + k, a0b + c), acc);
+        yb[m * 16 * 17 + r * 17 + c] = acc;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = fmaf(tf(b0b + r, b0b + k), yb[m * 16 * 17 + k * 17 + c], acc);
+        tf(b0b + r, a0b + c) = acc;
+      }
+      __syncthreads();
+      // the two halves: Y = A[32 + r][k] T[k][c], then T[32 + r][c] = T[32 + r][32 + k] Y[k][c]
+      {
+        const int c = tid & 31, r0 = tid >> 5;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int k = 0; k < 32; ++k) {
+          const float t = tf(k, c);
+#pragma unroll
+          for (int m = 0; m < 4; ++m) acc[m] = fmaf(As[(32 + r0 + 8 * m) * LDA + k], t, acc[m]);
         }
 #pragma unroll
-        for (int j = r & ~3; j < r; ++j) acc[j & 3] = fmaf(As[r * LDA + j], x[j], acc[j & 3]);
-        x[r] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-        *p = vcol ? x[r] : to_tf32(x[r]);  // U stays FP32; W becomes an operand
+        for (int m = 0; m < 4; ++m) yb[(r0 + 8 * m) * 33 + c] = acc[m];
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < 4; ++m) acc[m] = 0.f;
+#pragma unroll 4
+        for (int k = 0; k < 32; ++k) {
+          const float y = yb[k * 33 + c];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) acc[m] = fmaf(tf(32 + r0 + 8 * m, 32 + k), y, acc[m]);
+        }
+#pragma unroll
+        for (int m = 0; m < 4; ++m) tf(32 + r0 + 8 * m, c) = acc[m];
+      }
+      __syncthreads();
+      // T diag(beta), TF32: the A operand of MV
+#pragma unroll 4
+      for (int e = tid; e < C * C; e += kGdnThreads) {
+        const int r = e >> 6, c = e & 63;
+        float& t = tf(r, c);
+        t = to_tf32(t * bs[c]);
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // ---- M1: D1 = [W; q e^g] S ----
+    // ---- MV: D_V = [T diag(beta); 0] R ----
     if (tid == 32) {
       tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < DH / 8; ++kk) {
+      for (int kk = 0; kk < C / 8; ++kk) {
         const uint32_t aoff = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
-        umma_tf32(tmem + Sh::D1, smem_desc_k128(a0 + aoff), smem_desc_mn128_32b(ss_addr + kk * 1024, DH * 128),
-                  IDESC_S, kk > 0 ? 1u : 0u);
+        umma_tf32(tmem + Sh::DV, smem_desc_k128(st + aoff), smem_desc_mn128_32b(sv + kk * 1024, C * 128), IDESC_N,
+                  kk > 0 ? 1u : 0u);
       }
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
-    // ---- V: V_new = U - W S (rows 0-63), in place of U ----
+    // ---- V_new (lanes 0-63) -> the B operand tile, in place of R ----
     if (lrow < C) {
       const int c = lrow;
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
         uint32_t d[32];
         const int j0 = 64 * half + 32 * part;
-        tmem_ld32(tmem + t_lane + Sh::D1 + j0, d);
+        tmem_ld32(tmem + t_lane + Sh::DV + j0, d);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          float4* p = reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e, C));
-          float4 u = *p;
-          u.x = to_tf32(u.x - __uint_as_float(d[e]));
-          u.y = to_tf32(u.y - __uint_as_float(d[e + 1]));
-          u.z = to_tf32(u.z - __uint_as_float(d[e + 2]));
-          u.w = to_tf32(u.w - __uint_as_float(d[e + 3]));
-          *p = u;
-        }
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e, C)) =
+              make_float4(to_tf32(__uint_as_float(d[e])), to_tf32(__uint_as_float(d[e + 1])),
+                          to_tf32(__uint_as_float(d[e + 2])), to_tf32(__uint_as_float(d[e + 3])));
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // ---- M2: D1 += [. ; M] V_new;  M3: D2 = K~^T V_new ----
+    // ---- M3: D3 = M V_new (over the MV product);  M4: D2 = K~^T V_new ----
     if (tid == 32) {
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < C / 8; ++kk) {
         const uint64_t bdesc = smem_desc_mn128_32b(sv + kk * 1024, C * 128);
-        umma_tf32_ts(tmem + Sh::D1, tmem + Sh::D0 + kk * 8, bdesc, IDESC_V, 1u);
-        umma_tf32_ts(tmem + Sh::D2, tmem + Sh::KT + kk * 8, bdesc, IDESC_V, kk > 0 ? 1u : 0u);
+        umma_tf32_ts(tmem + Sh::DV, tmem + Sh::D0 + kk * 8, bdesc, IDESC_N, kk > 0 ? 1u : 0u);
+        umma_tf32_ts(tmem + Sh::D2, tmem + Sh::KT + kk * 8, bdesc, IDESC_N, kk > 0 ? 1u : 0u);
       }
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
-    // ---- S = S e^{g_last} + D2 (lane i = key dim, 64 value columns per thread) ----
+    // ---- S = S e^{g_last} + D2 (lane = key dim, 64 value columns per thread) ----
     {
       const float decay = es[C - 1];
 #pragma unroll
@@ -477,17 +546,20 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
         }
       }
     }
-    // ---- O: gated RMSNorm x SiLU(z) of the output rows (text.py:61-67) ----
+    // ---- O: rows e^g (q S) + M V_new, gated RMSNorm x SiLU(z) (text.py:61-67) ----
     if (lrow >= C) {
       const int c = lrow - C, t = t0 + c;
+      const float ec = es[c];
       float o[64];
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
-        uint32_t d[32];
+        uint32_t d[32], m[32];
         tmem_ld32(tmem + t_lane + Sh::D1 + 64 * half + 32 * part, d);
+        tmem_ld32(tmem + t_lane + Sh::DV + 64 * half + 32 * part, m);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[32 * part + e] = round_to<T>(__uint_as_float(d[e]));
+        for (int e = 0; e < 32; ++e)
+          o[32 * part + e] = round_to<T>(fmaf(ec, __uint_as_float(d[e]), __uint_as_float(m[e])));
       }
       float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
