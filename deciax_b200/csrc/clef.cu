@@ -446,6 +446,16 @@ static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
             done.insert(current_device());
           }
         }
+        REQUIRE(a.qkv_conv != nullptr && a.ldc >= static_cast<long long>(2 * a.nh + a.nv) * 128,
+                "the tensor-core Gated DeltaNet path needs the conv-pass buffer");
+        const int span = kGdnChunk * kGdnConvBlocks;
+        const dim3 cgrid((a.S + span - 1) / span, 2 * a.nh + a.nv, a.B);
+        if (a.width <= 4)
+          gdn_conv_bf16_kernel<4><<<cgrid, kGdnThreads, 0, L.stream>>>(a);
+        else
+          gdn_conv_bf16_kernel<8><<<cgrid, kGdnThreads, 0, L.stream>>>(a);
+        CUDA_CHECK(cudaGetLastError());
+        L.tick();
         gdn_tc_kernel<<<dim3(a.nv, a.B), kGdnThreads, GdnTcShape::SMEM, L.stream>>>(a);
         CUDA_CHECK(cudaGetLastError());
         L.tick();
@@ -665,6 +675,7 @@ struct Workspace {
   int b = 0, s = 0, lx = 0, o = 0, q = 0;
   DBuf ints, bytes;  // staged batch arrays (device)
   DBuf x, h, qkv, attn, gu, act, partial, gproj;
+  DBuf gconv;  // Gated DeltaNet conv pass output (bf16, head dim 128): [T, (2 nh_l + nv_l) dh]
   DBuf tp_flags;  // TP: tile flags of the fused GEMM + reduction (peers write them)
   DBuf memory, mnorm, kv;
   DBuf gv, questions, contexts, lexical;
@@ -685,6 +696,8 @@ struct Model {
   // Gated DeltaNet dims (global / this rank) and packed projection layout
   int g_nh = 0, g_nv = 0, g_dh = 0, g_width = 0, g_nh_l = 0, g_nv_l = 0, Ng = 0, Ng_pad = 0, Cg = 0;
   bool any_linear = false;
+  // BF16 Gated DeltaNet at head dim 128 runs the tensor-core kernel after a separate conv pass
+  bool gdn_conv_pass() const { return dtype == CLEF_DTYPE_BF16 && g_dh == 128; }
   bool finalized = false;
   std::string last_error;
   cudaStream_t stream = nullptr;
@@ -1368,6 +1381,7 @@ struct Model {
     grow(w.qkv, act_bytes(T * Nqkv));
     grow(w.attn, act_bytes(T * std::max(Hq_l * d, g_nv_l * g_dh)));
     if (any_linear) grow(w.gproj, act_bytes(T * Ng_pad));
+    if (any_linear && gdn_conv_pass()) grow(w.gconv, T * (2 * g_nh_l + g_nv_l) * g_dh * 2);
     if (dtype == CLEF_DTYPE_F32) grow(w.gu, act_bytes(T * 2 * Fp));
     grow(w.act, act_bytes(T * Fp));
     if (tp > 1) {
@@ -1612,6 +1626,10 @@ struct Model {
     a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(g_dh)));
     a.eps = cfg.rms_norm_eps;
     a.status = Lc.status;
+    if (gdn_conv_pass()) {
+      a.qkv_conv = ws.gconv.p;
+      a.ldc = static_cast<long long>(2 * g_nh_l + g_nv_l) * g_dh;
+    }
     Lc.cat = kCatGdn;
     launch_gdn<T>(Lc, a, g_dh);
     Lc.cat = kCatGemmO;
@@ -1622,7 +1640,7 @@ struct Model {
   // before it reads (not the staged batch, the flags or the status word).
   void poison_scratch(cudaStream_t st) {
     Workspace& w = ws;
-    for (DBuf* b : {&w.x, &w.h, &w.qkv, &w.attn, &w.gu, &w.act, &w.partial, &w.gproj, &w.memory, &w.mnorm, &w.kv,
+    for (DBuf* b : {&w.x, &w.h, &w.qkv, &w.attn, &w.gu, &w.act, &w.partial, &w.gproj, &w.gconv, &w.memory, &w.mnorm, &w.kv,
                     &w.gv, &w.questions, &w.contexts, &w.lexical, &w.small, &w.f32small})
       if (b->p) CUDA_CHECK(cudaMemsetAsync(b->p, 0xFF, b->bytes, st));
   }
@@ -2420,6 +2438,37 @@ int clef_op_attention(int dtype, const void* qkv, const uint8_t* mask, void* out
   });
 }
 
+}  // extern "C"
+
+namespace clef {
+// A stream-ordered memory pool of this library per device, for the scratch of
+// single-op entry points: it keeps its memory between calls (an allocation
+// after a synchronize does not map the memory again), and other users of the
+// device's default pool are not affected.  A device whose context was reset
+// and rebuilt gets a new pool (detected by its default pool's handle).
+static cudaMemPool_t op_scratch_pool(int device) {
+  static std::mutex mu;
+  static std::map<int, std::pair<cudaMemPool_t, cudaMemPool_t>> pools;  // device -> (default pool seen, ours)
+  std::lock_guard<std::mutex> lock(mu);
+  cudaMemPool_t def = nullptr;
+  CUDA_CHECK(cudaDeviceGetDefaultMemPool(&def, device));
+  auto it = pools.find(device);
+  if (it != pools.end() && it->second.first == def) return it->second.second;
+  cudaMemPoolProps props{};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = device;
+  cudaMemPool_t pool = nullptr;
+  CUDA_CHECK(cudaMemPoolCreate(&pool, &props));
+  uint64_t keep = ~0ull;
+  CUDA_CHECK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  pools[device] = {def, pool};
+  return pool;
+}
+}  // namespace clef
+
+extern "C" {
+
 int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int width, const void* A_log,
                      const void* dt_bias, const void* norm_w, void* out, int b, int s, int nh, int nv, int dh, float eps,
                      void* stream) {
@@ -2454,10 +2503,23 @@ int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int
     a.nv = nv;
     a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
     a.eps = eps;
-    if (dtype == CLEF_DTYPE_BF16)
+    if (dtype == CLEF_DTYPE_BF16 && dh == 128) {
+      // the conv pass's rows, stream-ordered: allocated and freed on the caller's stream
+      a.ldc = static_cast<long long>(2 * nh + nv) * dh;
+      const size_t bytes = static_cast<size_t>(b) * s * a.ldc * 2;
+      CUDA_CHECK(cudaMallocFromPoolAsync(&a.qkv_conv, bytes, clef::op_scratch_pool(clef::current_device()), L.stream));
+      try {
+        clef::launch_gdn<bf16>(L, a, dh);
+      } catch (...) {
+        cudaFreeAsync(a.qkv_conv, L.stream);
+        throw;
+      }
+      CUDA_CHECK(cudaFreeAsync(a.qkv_conv, L.stream));
+    } else if (dtype == CLEF_DTYPE_BF16) {
       clef::launch_gdn<bf16>(L, a, dh);
-    else
+    } else {
       clef::launch_gdn<float>(L, a, dh);
+    }
   });
 }
 

@@ -40,6 +40,9 @@ struct GdnArgs {
   float qscale;  // dk^-1/2 as a float32
   float eps;     // rms_norm_eps of the gated norm
   int* status;   // device status word for a bounded wait that gives up (tensor-core kernel); may be null
+  // tensor-core path only: the conv pass's bf16 rows [B*S, ldc] (q heads, k heads, v heads)
+  void* qkv_conv;
+  long long ldc;
 };
 
 constexpr int kGdnChunk = 64;

@@ -52,9 +52,11 @@ struct GdnTcShape {
   static constexpr uint32_t S_BYTES = DH * DH * 4;        // state, MN-major B [dk rows][dv]
   static constexpr uint32_t A0_BYTES = 2 * C * DH * 4;    // [k; q], K-major [128 rows][dk]
   static constexpr uint32_t V_BYTES = C * DH * 4;         // v -> R -> V_new, MN-major [tokens][dv]
-  static constexpr uint32_t T_BYTES = 2 * C * C * 4;      // T diag(beta), K-major [128 rows][64]; rows 64-127 zero
+  static constexpr uint32_t T_BYTES = 2 * C * C * 4;      // T diag(beta), K-major [128 rows][64]; rows 64-127 the unscaled T
   static constexpr uint32_t AS_BYTES = C * LDA * 4;       // system matrix, row-major
-  static constexpr uint32_t MISC_FLOATS = 4 * C + 3 * DH * 4 + 2 * C + 32 * 33;  // gates, conv taps, norm partial sums, inverse blocks
+  static constexpr uint32_t MISC_FLOATS = 4 * C + 2 * C + 32 * 33 + DH;  // gates, norm sums, inverse blocks, norm weight
+  static constexpr int ZLD = DH + 8;  // z rows staged over the system matrix: bf16, 272-byte rows
+  static_assert(C * ZLD * 2 <= AS_BYTES, "z staging");
   static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + AS_BYTES + MISC_FLOATS * 4 + 64;
   static constexpr uint32_t D0 = 0, D1 = 64, DV = 192, D2 = 320, KT = 448, TMEM_COLS = 512;
 };
@@ -123,98 +125,73 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-// Stage L: conv + SiLU (text.py:31-39), L2 norms of q and k (reference.py:14-21)
-// for rows t0..t0+63 into the operand tiles: k -> A0 rows 0-63, q (x dk^-1/2)
-// -> A0 rows 64-127, v -> V.  The sliding-window arithmetic is gdn_load_chunk's
-// (same taps, same order of operations), only the stores differ.
+// Stage L as its own pass: causal conv + SiLU (text.py:31-39) of every q, k
+// and v channel and the L2 norms of q and k (reference.py:14-21), written as
+// bf16 rows [B*S, 2*nh*dh + nv*dh] (q heads, k heads, v heads, in projection
+// column order).  Every value is one the reference rounds to bf16, so the
+// chunk kernel reads exactly what it used to compute itself; q leaves without
+// the dk^-1/2 factor.  One CTA per (256-token span, q/k/v head, state): the
+// q and k heads are computed once, not once per value head that shares them,
+// and the pass runs at full occupancy (each CTA walks kGdnConvBlocks blocks
+// with its taps in registers).  The sliding-window arithmetic is
+// gdn_load_chunk's (same taps, same order of operations).
+constexpr int kGdnConvBlocks = 4;  // 64-token blocks per CTA of the conv pass
+
 template <int W>
-__device__ __forceinline__ void gdn_tc_load_chunk(const GdnArgs& a, const __nv_bfloat16* proj,
-                                                  const __nv_bfloat16* convw, const float* wsm, long long row0, int t0,
-                                                  int q_col, int k_col, int v_col, uint8_t* sA0, uint8_t* sV) {
+__global__ void __launch_bounds__(kGdnThreads) gdn_conv_bf16_kernel(GdnArgs a) {
   using T = __nv_bfloat16;
   constexpr int C = kGdnChunk, DH = kGdnTcDim, VN = GdnVec<T>::N, GL = DH / VN, RPP = kGdnThreads / GL;
   constexpr int RT = C / RPP, NX = RT + W - 1;
   const int tid = threadIdx.x, g = tid % GL, r0 = (tid / GL) * RT;
+  const int kh = blockIdx.y, b = blockIdx.z;
+  const int kind = kh < a.nh ? 0 : kh < 2 * a.nh ? 1 : 2;
+  const int col = (kind == 0 ? kh * DH : kind == 1 ? a.k_col + (kh - a.nh) * DH : a.v_col + (kh - 2 * a.nh) * DH) +
+                  g * VN;
+  const T* proj = static_cast<const T*>(a.proj);
+  const T* convw = static_cast<const T*>(a.conv);
+  T* dst = static_cast<T*>(a.qkv_conv);
+  const long long row0 = static_cast<long long>(b) * a.S;
   const int shift = W - a.width;
-  constexpr int NK = W <= 4 ? 3 : 1;
-  uint4 raw[NK][NX];
-  auto load_kind = [&](int kind, uint4 (&dst)[NX]) {
-    const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + g * VN;
+  float w[VN][W];  // this thread's taps, loaded once for all its blocks
 #pragma unroll
-    for (int i = 0; i < NX; ++i) {
-      const int tt = t0 + r0 - (W - 1) + i;
-      dst[i] = (tt >= 0 && tt < a.S) ? *reinterpret_cast<const uint4*>(proj + (row0 + tt) * a.ldp + col)
-                                     : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  if constexpr (NK == 3) {
+  for (int c = 0; c < VN; ++c)
 #pragma unroll
-    for (int kind = 0; kind < 3; ++kind) load_kind(kind, raw[kind]);
-  }
-#pragma unroll
-  for (int kind = 0; kind < 3; ++kind) {
-    const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + g * VN;
-    if constexpr (NK == 1) load_kind(kind, raw[0]);
-    const uint4 (&rk)[NX] = raw[NK == 3 ? kind : 0];
-    float w[VN][W];
-    if (wsm) {  // taps staged [kind][tap][channel]: 16-byte reads of 4 channels, no bank conflicts
-#pragma unroll
-      for (int i = 0; i < W; ++i)
-#pragma unroll
-        for (int c = 0; c < VN; c += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(wsm + (kind * W + i) * DH + g * VN + c);
-          w[c][i] = t4.x;
-          w[c + 1][i] = t4.y;
-          w[c + 2][i] = t4.z;
-          w[c + 3][i] = t4.w;
-        }
-    } else {
-#pragma unroll
-      for (int c = 0; c < VN; ++c)
-#pragma unroll
-        for (int i = 0; i < W; ++i)
-          w[c][i] = i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f;
-    }
+    for (int i = 0; i < W; ++i)
+      w[c][i] = i >= shift ? to_f32(convw[static_cast<long long>(col + c) * a.width + (i - shift)]) : 0.f;
+  for (int blk = 0; blk < kGdnConvBlocks; ++blk) {
+    const int t0 = (blockIdx.x * kGdnConvBlocks + blk) * C;  // uniform across the CTA
+    if (t0 >= a.S) break;
     float x[NX][VN];
 #pragma unroll
     for (int i = 0; i < NX; ++i) {
-      const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&rk[i]);
+      const int tt = t0 + r0 - (W - 1) + i;
+      const uint4 raw = (tt >= 0 && tt < a.S) ? *reinterpret_cast<const uint4*>(proj + (row0 + tt) * a.ldp + col)
+                                              : make_uint4(0u, 0u, 0u, 0u);
+      const T* hv = reinterpret_cast<const T*>(&raw);
 #pragma unroll
       for (int c = 0; c < VN; ++c) x[i][c] = __bfloat162float(hv[c]);
     }
 #pragma unroll
     for (int j = 0; j < RT; ++j) {
-      const int r = r0 + j;
-      float y[VN];
+      const int t = t0 + r0 + j;
+      GdnVec<T> y;
 #pragma unroll
       for (int c = 0; c < VN; ++c) {
         float acc = 0.f;
 #pragma unroll
         for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(x[j + i][c], w[c][i]));
         const float z = round_to<T>(acc);
-        y[c] = t0 + r < a.S ? round_to<T>(z * sigmoid_fast(z)) : 0.f;
+        y.v[c] = t < a.S ? round_to<T>(z * sigmoid_fast(z)) : 0.f;
       }
       if (kind < 2) {
         float ss = 0.f;
 #pragma unroll
-        for (int c = 0; c < VN; ++c) ss += y[c] * y[c];
+        for (int c = 0; c < VN; ++c) ss += y.v[c] * y.v[c];
         const float inv = rsqrtf(group_sum<GL>(ss) + 1e-6f);
-        const float scale = kind == 0 ? a.qscale : 1.f;
 #pragma unroll
-        for (int c = 0; c < VN; ++c) y[c] = round_to<T>(y[c] * inv) * scale;
-        if (kind == 0) {  // q x dk^-1/2 is an MMA operand: TF32 (k is bf16, exact in TF32)
-#pragma unroll
-          for (int c = 0; c < VN; ++c) y[c] = to_tf32(y[c]);
-        }
+        for (int c = 0; c < VN; ++c) y.v[c] = round_to<T>(y.v[c] * inv);
       }
-#pragma unroll
-      for (int c = 0; c < VN; c += 4) {
-        const float4 v4 = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
-        if (kind == 2)
-          *reinterpret_cast<float4*>(sV + gdn_sw_mn(r, g * VN + c, C)) = v4;
-        else
-          *reinterpret_cast<float4*>(sA0 + gdn_sw(kind == 0 ? C + r : r, g * VN + c, 2 * C)) = v4;
-      }
+      if (t < a.S) y.store(dst + (row0 + t) * a.ldc + kh * DH + g * VN);
     }
   }
 }
@@ -237,10 +214,10 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   float* bs = gs + C;                                      // beta
   float* es = bs + C;                                      // e^g
   float* ws = es + C;                                      // e^(g_last - g)
-  float* wconv = ws + C;                                   // [3][4][DH] conv taps (width <= 4)
-  float* red = wconv + 3 * DH * 4;                         // [2][C] output-row partial sums of squares
+  float* red = ws + C;                                     // [2][C] output-row partial sums of squares
   float* yb = red + 2 * C;                                 // [32][33] products of the blocked inverse
-  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(yb + 32 * 33);
+  float* nws = yb + 32 * 33;                               // gated-norm weight
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(nws + DH);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
 
   const int h = blockIdx.x, b = blockIdx.y;
@@ -250,13 +227,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
   const int hk = h / (a.nv / a.nh);
   const T* proj = static_cast<const T*>(a.proj);
-  const T* convw = static_cast<const T*>(a.conv);
   const T* nw = static_cast<const T*>(a.norm_w);
+  const T* qkv = static_cast<const T*>(a.qkv_conv);
   T* out = static_cast<T*>(a.out);
   const float neg_a = -expf(to_f32(static_cast<const T*>(a.A_log)[h]));
   const float dt_bias = to_f32(static_cast<const T*>(a.dt_bias)[h]);
   const long long row0 = static_cast<long long>(b) * a.S;
-  const int q_col = hk * DH, k_col = a.k_col + hk * DH, v_col = a.v_col + h * DH;
+  const int q_col = hk * DH, k_col = (a.nh + hk) * DH, v_col = (2 * a.nh + h) * DH;  // columns of the conv pass
 
   if (tid == 0) {
     mbar_init(mma_bar, 1);
@@ -267,16 +244,9 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     tmem_relinquish();
   }
   for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
-  // rows 64-127 of the T operand stay zero: the MV product's lanes 64-127 are unused
+  // the T tile starts zero: blocks above the diagonal are never written
   for (int i = tid; i < 2 * C * C; i += kGdnThreads) reinterpret_cast<float*>(sT)[i] = 0.f;
-  if (a.width <= 4) {
-    const int shift = 4 - a.width;
-    for (int i = tid; i < 3 * DH * 4; i += kGdnThreads) {  // [kind][tap][channel]
-      const int kind = i / (DH * 4), tap = (i / DH) % 4, c = i % DH;
-      const int col = (kind == 0 ? q_col : kind == 1 ? k_col : v_col) + c;
-      wconv[i] = tap >= shift ? to_f32(convw[static_cast<long long>(col) * a.width + (tap - shift)]) : 0.f;
-    }
-  }
+  if (tid < DH) nws[tid] = to_f32(nw[tid]);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -295,8 +265,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   const int chunks = (a.S + C - 1) / C;
   for (int ci = 0; ci < chunks; ++ci) {
     const int t0 = ci * C;
-    // ---- L: conv + SiLU, L2 norms, gates (the gate inputs are loaded first,
-    // so their latency overlaps the convolution) ----
+    // ---- L: q, k, v rows of the conv pass into the operand tiles (k -> A0
+    // rows 0-63, q x dk^-1/2 -> A0 rows 64-127, v -> V), and the gates ----
     float ga = 0.f, gb = 0.f;
     const bool gate_row = tid < C && t0 + tid < a.S;
     if (gate_row) {
@@ -304,10 +274,38 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       ga = to_f32(pr[a.a_col + h]);
       gb = to_f32(pr[a.b_col + h]);
     }
-    if (a.width <= 4)
-      gdn_tc_load_chunk<4>(a, proj, convw, wconv, row0, t0, q_col, k_col, v_col, sA0, sV);
-    else
-      gdn_tc_load_chunk<8>(a, proj, convw, nullptr, row0, t0, q_col, k_col, v_col, sA0, sV);
+    {
+      constexpr int RS = kGdnThreads / 16;  // rows per pass: 16 threads x 8 channels per row
+      uint4 raw[3][C / RS];
+#pragma unroll
+      for (int i = 0; i < C / RS; ++i) {
+        const int r = tid / 16 + RS * i, t = t0 + r, g8 = (tid % 16) * 8;
+        const T* src = qkv + (row0 + t) * a.ldc + g8;
+#pragma unroll
+        for (int kind = 0; kind < 3; ++kind)
+          raw[kind][i] = t < a.S ? *reinterpret_cast<const uint4*>(src + (kind == 0 ? q_col : kind == 1 ? k_col : v_col))
+                                 : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int i = 0; i < C / RS; ++i) {
+        const int r = tid / 16 + RS * i, g8 = (tid % 16) * 8;
+#pragma unroll
+        for (int kind = 0; kind < 3; ++kind) {
+          const T* hv = reinterpret_cast<const T*>(&raw[kind][i]);
+          float y[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) y[c] = kind == 0 ? to_tf32(__bfloat162float(hv[c]) * a.qscale) : __bfloat162float(hv[c]);
+#pragma unroll
+          for (int c = 0; c < 8; c += 4) {
+            const float4 v4 = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
+            if (kind == 2)
+              *reinterpret_cast<float4*>(sV + gdn_sw_mn(r, g8 + c, C)) = v4;
+            else
+              *reinterpret_cast<float4*>(sA0 + gdn_sw(kind == 0 ? C + r : r, g8 + c, 2 * C)) = v4;
+          }
+        }
+      }
+    }
     if (tid < C) {
       gs[tid] = gate_row ? neg_a * softplus_f(ga + dt_bias) : 0.f;
       bs[tid] = gate_row ? round_to<T>(sigmoid_fast(gb)) : 0.f;
@@ -399,14 +397,24 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       tmem_wait_st();
     }
     __syncthreads();
-    // ---- T: (I - A)^{-1} by blocks, in the T operand tile (rows 0-63), then
-    // scaled by beta per column and rounded to TF32.  Diagonal 16 x 16 blocks by
+    // ---- T: (I - A)^{-1} by blocks.  The unscaled inverse is built in rows
+    // 64-127 of the T tile (rows the MV product computes but nobody reads);
+    // each block, once final, also goes to rows 0-63 scaled by beta per column
+    // and rounded to TF32: the A operand of MV.  Diagonal 16 x 16 blocks by
     // forward substitution; then for [[P, 0], [Q, R]] with known inverses P', R'
     // the lower-left block of the inverse is R' (Q~ P'), Q~ = the system
     // entries (A holds minus the matrix's off-diagonal), first for the 16 x 16
-    // pairs of blocks, then for the two 32 x 32 halves ----
+    // pairs of blocks, then for the two 32 x 32 halves.  Blocks above the
+    // diagonal are never written and stay zero in both copies. ----
     {
-      auto tf = [&](int r, int c) -> float& { return *reinterpret_cast<float*>(sT + gdn_sw(r, c, 2 * C)); };
+      auto tw = [&](int r, int c) -> float& { return *reinterpret_cast<float*>(sT + gdn_sw(C + r, c, 2 * C)); };
+      auto tw4 = [&](int r, int c4) -> float4 {  // working row r, columns c4..c4+3
+        return *reinterpret_cast<const float4*>(sT + gdn_sw(C + r, c4, 2 * C));
+      };
+      auto put = [&](int r, int c, float v) {
+        tw(r, c) = v;
+        *reinterpret_cast<float*>(sT + gdn_sw(r, c, 2 * C)) = to_tf32(v * bs[c]);
+      };
       if (tid < C) {
         const int b0 = (tid >> 4) * 16, c = tid & 15;
         float x[16];
@@ -422,7 +430,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
               acc0 = fmaf(arow[j], x[j], acc0);
           }
           x[r] = acc0 + acc1;
-          tf(b0 + r, b0 + c) = x[r];
+          put(b0 + r, b0 + c, x[r]);
         }
       }
       __syncthreads();
@@ -433,7 +441,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
         const float* arow = As + (b0b + r) * LDA + a0b;
         float acc = 0.f;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc = fmaf(arow[k], tf(a0b + k, a0b + c), acc);
+        for (int k4 = 0; k4 < 16; k4 += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(arow + k4);
+          acc = fmaf(a4.x, tw(a0b + k4, a0b + c), acc);
+          acc = fmaf(a4.y, tw(a0b + k4 + 1, a0b + c), acc);
+          acc = fmaf(a4.z, tw(a0b + k4 + 2, a0b + c), acc);
+          acc = fmaf(a4.w, tw(a0b + k4 + 3, a0b + c), acc);
+        }
         yb[m * 16 * 17 + r * 17 + c] = acc;
       }
       __syncthreads();
@@ -442,47 +456,71 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
         const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
         float acc = 0.f;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) acc = fmaf(tf(b0b + r, b0b + k), yb[m * 16 * 17 + k * 17 + c], acc);
-        tf(b0b + r, a0b + c) = acc;
+        for (int k4 = 0; k4 < 16; k4 += 4) {
+          const float4 t4 = tw4(b0b + r, b0b + k4);
+          acc = fmaf(t4.x, yb[m * 16 * 17 + k4 * 17 + c], acc);
+          acc = fmaf(t4.y, yb[m * 16 * 17 + (k4 + 1) * 17 + c], acc);
+          acc = fmaf(t4.z, yb[m * 16 * 17 + (k4 + 2) * 17 + c], acc);
+          acc = fmaf(t4.w, yb[m * 16 * 17 + (k4 + 3) * 17 + c], acc);
+        }
+        put(b0b + r, a0b + c, acc);
       }
       __syncthreads();
       // the two halves: Y = A[32 + r][k] T[k][c], then T[32 + r][c] = T[32 + r][32 + k] Y[k][c]
       {
         const int c = tid & 31, r0 = tid >> 5;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int k = 0; k < 32; ++k) {
-          const float t = tf(k, c);
 #pragma unroll
-          for (int m = 0; m < 4; ++m) acc[m] = fmaf(As[(32 + r0 + 8 * m) * LDA + k], t, acc[m]);
+        for (int k4 = 0; k4 < 32; k4 += 4) {
+          float t[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) t[e] = tw(k4 + e, c);
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const float4 a4 = *reinterpret_cast<const float4*>(As + (32 + r0 + 8 * m) * LDA + k4);
+            acc[m] = fmaf(a4.x, t[0], acc[m]);
+            acc[m] = fmaf(a4.y, t[1], acc[m]);
+            acc[m] = fmaf(a4.z, t[2], acc[m]);
+            acc[m] = fmaf(a4.w, t[3], acc[m]);
+          }
         }
 #pragma unroll
         for (int m = 0; m < 4; ++m) yb[(r0 + 8 * m) * 33 + c] = acc[m];
         __syncthreads();
 #pragma unroll
         for (int m = 0; m < 4; ++m) acc[m] = 0.f;
-#pragma unroll 4
-        for (int k = 0; k < 32; ++k) {
-          const float y = yb[k * 33 + c];
 #pragma unroll
-          for (int m = 0; m < 4; ++m) acc[m] = fmaf(tf(32 + r0 + 8 * m, 32 + k), y, acc[m]);
+        for (int k4 = 0; k4 < 32; k4 += 4) {
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[e] = yb[(k4 + e) * 33 + c];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const float4 t4 = tw4(32 + r0 + 8 * m, 32 + k4);
+            acc[m] = fmaf(t4.x, y[0], acc[m]);
+            acc[m] = fmaf(t4.y, y[1], acc[m]);
+            acc[m] = fmaf(t4.z, y[2], acc[m]);
+            acc[m] = fmaf(t4.w, y[3], acc[m]);
+          }
         }
 #pragma unroll
-        for (int m = 0; m < 4; ++m) tf(32 + r0 + 8 * m, c) = acc[m];
-      }
-      __syncthreads();
-      // T diag(beta), TF32: the A operand of MV
-#pragma unroll 4
-      for (int e = tid; e < C * C; e += kGdnThreads) {
-        const int r = e >> 6, c = e & 63;
-        float& t = tf(r, c);
-        t = to_tf32(t * bs[c]);
+        for (int m = 0; m < 4; ++m) put(32 + r0 + 8 * m, c, acc[m]);
       }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // ---- MV: D_V = [T diag(beta); 0] R ----
+    // the system matrix is done with: each output thread stages its z row
+    // segment (64 bf16) there for the O phase
+    if (lrow >= C) {
+      const int c = lrow - C, t = t0 + c;
+      const T* src = proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + 64 * half;
+      T* dst = reinterpret_cast<T*>(As) + c * Sh::ZLD + 64 * half;
+#pragma unroll
+      for (int e8 = 0; e8 < 64; e8 += 8) cp_async16(dst + e8, src + e8, t < a.S);
+      cp_async_commit();
+    }
+    // ---- MV: D_V = [T diag(beta); T] R (lanes 64-127 unused) ----
     if (tid == 32) {
       tc_fence_after();
 #pragma unroll
@@ -525,6 +563,39 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
+    // ---- O1 (lanes 64-127): o = T(e^g (q S) + M V_new) into the A0 tile, which
+    // no MMA reads any more this chunk (rows of 132 floats), and each row
+    // half's sum of squares ----
+    constexpr int OLD = DH + 4;
+    float* ob = reinterpret_cast<float*>(sA0);
+    if (lrow >= C) {
+      const int c = lrow - C;
+      const float ec = es[c];
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        uint32_t d[32], m[32];
+        const int j0 = 64 * half + 32 * part;
+        tmem_ld32(tmem + t_lane + Sh::D1 + j0, d);
+        tmem_ld32(tmem + t_lane + Sh::DV + j0, m);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          float4 o4;
+          o4.x = round_to<T>(fmaf(ec, __uint_as_float(d[e]), __uint_as_float(m[e])));
+          o4.y = round_to<T>(fmaf(ec, __uint_as_float(d[e + 1]), __uint_as_float(m[e + 1])));
+          o4.z = round_to<T>(fmaf(ec, __uint_as_float(d[e + 2]), __uint_as_float(m[e + 2])));
+          o4.w = round_to<T>(fmaf(ec, __uint_as_float(d[e + 3]), __uint_as_float(m[e + 3])));
+          sq[0] = fmaf(o4.x, o4.x, sq[0]);
+          sq[1] = fmaf(o4.y, o4.y, sq[1]);
+          sq[2] = fmaf(o4.z, o4.z, sq[2]);
+          sq[3] = fmaf(o4.w, o4.w, sq[3]);
+          *reinterpret_cast<float4*>(ob + c * OLD + j0 + e) = o4;
+        }
+      }
+      red[half * C + c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
+      cp_async_wait<0>();  // this thread's z copies, read by others after the barrier
+    }
     // ---- S = S e^{g_last} + D2 (lane = key dim, 64 value columns per thread) ----
     {
       const float decay = es[C - 1];
@@ -546,38 +617,26 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
         }
       }
     }
-    // ---- O: rows e^g (q S) + M V_new, gated RMSNorm x SiLU(z) (text.py:61-67) ----
-    if (lrow >= C) {
-      const int c = lrow - C, t = t0 + c;
-      const float ec = es[c];
-      float o[64];
-#pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        uint32_t d[32], m[32];
-        tmem_ld32(tmem + t_lane + Sh::D1 + 64 * half + 32 * part, d);
-        tmem_ld32(tmem + t_lane + Sh::DV + 64 * half + 32 * part, m);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          o[32 * part + e] = round_to<T>(fmaf(ec, __uint_as_float(d[e]), __uint_as_float(m[e])));
-      }
-      float sq[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int e = 0; e < 64; ++e) sq[e & 3] = fmaf(o[e], o[e], sq[e & 3]);
-      red[half * C + c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 2, 3, 6, 7
-      const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
+    __syncthreads();
+    // ---- O2 (all threads, one row per lane, 32 columns per warp quarter of
+    // the CTA): gated RMSNorm x SiLU(z) (text.py:61-67) ----
+    {
+      const int c = tid & (C - 1), q32 = (tid >> 6) * 32, t = t0 + c;
       if (t < a.S) {
-        const T* zrow = proj + (row0 + t) * a.ldp + a.z_col + h * DH + 64 * half;
-        T* orow = out + (row0 + t) * a.ldo + h * DH + 64 * half;
+        const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
+        const T* zrow = reinterpret_cast<const T*>(As) + c * Sh::ZLD + q32;
+        const float* orow_s = ob + c * OLD + q32;
+        T* orow = out + (row0 + t) * a.ldo + h * DH + q32;
 #pragma unroll
-        for (int e8 = 0; e8 < 64; e8 += 8) {
-          GdnVec<T> z, wv, res;
+        for (int e8 = 0; e8 < 32; e8 += 8) {
+          GdnVec<T> z, res;
           z.load(zrow + e8);
-          wv.load(nw + 64 * half + e8);
+          const float4 o0 = *reinterpret_cast<const float4*>(orow_s + e8);
+          const float4 o1 = *reinterpret_cast<const float4*>(orow_s + e8 + 4);
+          const float o[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float n = round_to<T>(round_to<T>(o[e8 + e] * rs) * wv.v[e]);
+            const float n = round_to<T>(round_to<T>(o[e] * rs) * nws[q32 + e8 + e]);
             res.v[e] = n * (z.v[e] * sigmoid_fast(z.v[e]));
           }
           res.store(orow + e8);
