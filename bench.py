@@ -918,15 +918,50 @@ def serving_arm(args) -> None:
         sweep, questions = serving_records(lengths[rank::world], CFG2["vocab_size"], seed=10 + rank)
         longs = longs[rank::world]
         model = build_model(local, max_seq_len=c["max"])
-    engine = ClefEngine(model)
 
-    def run(records, timings=None):
+    def run(records, timings=None, eng=None):
         if dist:
             dist.barrier()
         t0 = time.perf_counter()
-        answers = engine.decide_records(records, questions, timings) if records else []
+        answers = (eng or engine).decide_records(records, questions, timings) if records else []
         elapsed = time.perf_counter() - t0
         return answers, elapsed
+
+    def pct(vals, q):
+        return float(np.percentile(np.asarray(vals) * 1e3, q)) if vals else 0.0
+
+    def first_sweep(m, warm: bool) -> dict:
+        """The first sweep a fresh model serves: after ClefEngine.warmup (the
+        server's warm-up request) or cold, its workspace growing with each new
+        batch shape."""
+        eng = ClefEngine(m, auto_warmup=warm)
+        warm_s = 0.0
+        if warm:
+            if dist:
+                dist.barrier()
+            t0 = time.perf_counter()
+            eng.warmup()
+            warm_s = time.perf_counter() - t0
+        before = m.workspace_allocations
+        timings = []
+        _, s = run(sweep, timings, eng)
+        return {"warmup_seconds": rank_reduce(warm_s, "max"), "sweep_seconds": rank_reduce(s, "max"),
+                "batch_latency_ms": {"p50": rank_reduce(pct([t for *_, t in timings], 50), "max"),
+                                     "p99": rank_reduce(pct([t for *_, t in timings], 99), "max"),
+                                     "max": rank_reduce(pct([t for *_, t in timings], 100), "max")},
+                "workspace_allocations_during_sweep": int(rank_reduce(float(m.workspace_allocations - before), "max"))}
+
+    # a second, fresh model serves its first sweep cold, then is released
+    if tp > 1:
+        cold_model = build_model(local, max_seq_len=c["max"], tp_rank=rank, tp_size=tp,
+                                 nccl_id=share_from_rank0(nccl_unique_id))
+    else:
+        cold_model = build_model(local, max_seq_len=c["max"])
+    cold = first_sweep(cold_model, warm=False)
+    cold_model.close()
+    del cold_model
+    warmed = first_sweep(model, warm=True)
+    engine = ClefEngine(model)
 
     for _ in range(args.warmup):
         run(sweep)
@@ -940,9 +975,6 @@ def serving_arm(args) -> None:
     assert all(len(a["answers"]) == QUESTIONS for a in answers)
 
     agg = rank_reduce
-
-    def pct(vals, q):
-        return float(np.percentile(np.asarray(vals) * 1e3, q)) if vals else 0.0
 
     sweep_s = agg(statistics.mean(sweep_t), "max")
     long_s = agg(statistics.mean(long_t), "max")
@@ -965,6 +997,7 @@ def serving_arm(args) -> None:
                        "batching": "ClefEngine length-grouped, max_batch_tokens 65536"},
             "prefill_tokens_per_s": tokens / sweep_s, "sweep_seconds": sweep_s,
             "batch_latency_ms": {"p50": p50, "p99": p99, "batches_per_rank": len(timings) // max(args.steps, 1)},
+            "first_sweep": {"after_warmup": warmed, "cold": cold},
             "max_len_case": {"states": c["long"], "tokens_per_state": c["max"], "seconds": long_s,
                              "decisions_per_s": c["long"] * QUESTIONS / long_s, "batch_latency_ms_p50": lp50},
             "timing": "host wall clock around ClefEngine.decide_records (collate, H2D, forward, D2H, decode)",

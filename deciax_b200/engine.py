@@ -95,14 +95,18 @@ def plan_batches(lengths: Sequence[int], max_batch_tokens: int = DEFAULT_BATCH_T
 
 class ClefEngine:
     def __init__(self, model: Any, *, replicas: Sequence[Any] | None = None,
-                 max_batch_tokens: int = DEFAULT_BATCH_TOKENS) -> None:
+                 max_batch_tokens: int = DEFAULT_BATCH_TOKENS, auto_warmup: bool = True) -> None:
+        """``auto_warmup=False`` skips the workspace reservation before the
+        first forward: the workspace then grows with each new batch shape (the
+        cold-start behaviour, for callers that bound device memory themselves
+        or that call ``warmup`` at a time of their choosing)."""
         self.model = model
         self.replicas = list(replicas) if replicas else [model]
         if max_batch_tokens < 1:
             raise ValueError("max_batch_tokens must be positive")
         self.max_batch_tokens = max_batch_tokens
         self._locks = [threading.Lock() for _ in self.replicas]
-        self._warm = False
+        self._warm = not auto_warmup
         self._warm_lock = threading.Lock()
 
     def warmup(self) -> None:

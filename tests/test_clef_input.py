@@ -258,6 +258,28 @@ def test_engine_matches_per_record_answers_in_input_order():
     assert len(model.calls) < len(ss) // 2  # larger batches than the reference's fixed pairs
 
 
+class WarmCountingReplica(FakeReplica):
+    def __init__(self, tokenizer):
+        super().__init__(tokenizer)
+        self.warmups: list[dict] = []
+
+    def warmup(self, **kw):
+        self.warmups.append(kw)
+
+
+def test_engine_warms_every_replica_once_before_the_first_forward():
+    questions = FIX["schemas"]["reference_test"]
+    replicas = [WarmCountingReplica(TOK) for _ in range(2)]
+    engine = ClefEngine(replicas[0], replicas=replicas, max_batch_tokens=4096)
+    engine.decide_batch(states(3), questions)
+    engine.decide_batch(states(5), questions)
+    assert [len(r.warmups) for r in replicas] == [1, 1]
+    assert replicas[0].warmups[0] == {"max_batch_tokens": 4096, "max_rows": I.ROW_BUCKETS[-1]}
+    cold = WarmCountingReplica(TOK)
+    ClefEngine(cold, auto_warmup=False).decide_batch(states(3), questions)
+    assert cold.warmups == [] and cold.calls  # served without a reservation
+
+
 def test_engine_data_parallel_replicas_run_concurrently():
     questions = FIX["schemas"]["reference_test"]
     replicas = [FakeReplica(TOK, delay=0.05) for _ in range(4)]
