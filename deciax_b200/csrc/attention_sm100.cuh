@@ -55,14 +55,21 @@ struct AttnTcArgs {
 
 template <int D>
 struct AttnTcShape {
-  static constexpr int BQ = 128, BK = 64, ATOMS = D / 64;
-  static constexpr bool P_TMEM = D == 128;             // P over its S buffer in tensor memory
+  // Key tile BK: 128 at head_dim 256 (QK^T at N = 128, full rate; two 128-column
+  // S buffers and the 256-column O fill the 512 tensor-memory columns, and
+  // Q + one K + one V stage fill shared memory), 64 otherwise.
+  static constexpr int BQ = 128, BK = D == 256 ? 128 : 64, ATOMS = D / 64;
+  static constexpr int KST = D == 256 ? 1 : 2;         // K and V stages each
+  static constexpr bool P_TMEM = D >= 128;             // P over its S buffer in tensor memory
   static constexpr uint32_t Q_BYTES = BQ * D * 2;      // ATOMS x [128 rows x 128 B]
-  static constexpr uint32_t KV_BYTES = BK * D * 2;     // ATOMS x [64 rows x 128 B]
-  static constexpr uint32_t P_BYTES = BQ * BK * 2;     // [128 rows x 128 B]
+  static constexpr uint32_t KV_BYTES = BK * D * 2;     // ATOMS x [BK rows x 128 B]
+  static constexpr uint32_t P_BYTES = BQ * BK * 2;     // [128 rows x 2 BK B]
   static constexpr uint32_t TMEM_COLS = D + 2 * BK <= 256 ? 256 : 512;
-  static constexpr uint32_t S_COL = 0, O_COL = 2 * BK;  // S buffers at 0 and 64, O at 128
-  static constexpr size_t SMEM = 1024 + Q_BYTES + 4 * KV_BYTES + (P_TMEM ? 0 : 2 * P_BYTES) + 256;
+  static constexpr uint32_t S_COL = 0, O_COL = 2 * BK;  // S buffers at 0 and BK, O after them
+  static constexpr size_t SMEM = 1024 + Q_BYTES + 2 * KST * KV_BYTES + (P_TMEM ? 0 : 2 * P_BYTES) + 256;
+  static_assert(D + 2 * BK <= 512, "tensor memory");
+  static_assert(Q_BYTES <= KST * KV_BYTES, "the gate tile is prefetched into the K stages");
+  static_assert(P_TMEM || BK == 64, "P through shared memory is laid out for 64-key tiles");
 };
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -96,7 +103,7 @@ template <int D>
 __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_out, AttnTcArgs a) {
   using Sh = AttnTcShape<D>;
-  constexpr int BQ = Sh::BQ, BK = Sh::BK, ATOMS = Sh::ATOMS;
+  constexpr int BQ = Sh::BQ, BK = Sh::BK, ATOMS = Sh::ATOMS, KST = Sh::KST, NW = BK / 32;
   constexpr uint32_t IDESC_QK = idesc_bf16_f32(BQ, BK);
   constexpr uint32_t IDESC_PV = idesc_bf16_f32(BQ, D) | (1u << 16);  // B (V) is MN-major
   constexpr float LOG2E = 1.4426950408889634f;
@@ -104,9 +111,9 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + Sh::Q_BYTES;        // 2 stages
-  uint8_t* sV = sK + 2 * Sh::KV_BYTES;   // 2 stages
-  uint8_t* sP = sV + 2 * Sh::KV_BYTES;   // 2 buffers (none when P lives in tensor memory)
+  uint8_t* sK = sQ + Sh::Q_BYTES;          // KST stages
+  uint8_t* sV = sK + KST * Sh::KV_BYTES;   // KST stages
+  uint8_t* sP = sV + KST * Sh::KV_BYTES;   // 2 buffers (none when P lives in tensor memory)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + (Sh::P_TMEM ? 0 : 2 * Sh::P_BYTES));
   uint64_t* qfull = bars;
   uint64_t* kfull = bars + 1;
@@ -162,41 +169,45 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
           tma_load_2d(sQ + at * (BQ * 128) + half * (64 * 128), &tmap, qfull, a.q_col + h * a.hsq + at * 64,
                       row_base + q0 + half * 64);
       // K runs one tile ahead of V: a K stage frees when its QK^T is done,
-      // a V stage only after the (later) P.V of the tile two back.
+      // a V stage only after the (later) P.V that reads it.  Tile i uses
+      // stage i % KST in phase (i / KST) & 1; each stage is BK / 64 boxes of
+      // 64 rows per 64-column atom.
       int nk = 0, nv = 0;  // tiles whose K / V load has been issued
       for (int i = 0; i <= n && !*abort_flag; ++i) {
         if (i < n) {
-          const int s = i & 1;
-          if (!mbar_wait(&kempty[s], ((i >> 1) & 1) ^ 1, a.status, kTimeoutAttention)) {
+          const int s = i % KST;
+          if (!mbar_wait(&kempty[s], ((i / KST) & 1) ^ 1, a.status, kTimeoutAttention)) {
             *abort_flag = 1;
             break;
           }
           mbar_arrive_expect_tx(&kfull[s], Sh::KV_BYTES);
           for (int at = 0; at < ATOMS; ++at)
-            tma_load_2d(sK + s * Sh::KV_BYTES + at * (BK * 128), &tmap, &kfull[s], a.k_col + hk * a.hsk + at * 64,
-                        row_base + (kb_lo + i) * BK);
+            for (int bx = 0; bx < BK / 64; ++bx)
+              tma_load_2d(sK + s * Sh::KV_BYTES + at * (BK * 128) + bx * (64 * 128), &tmap, &kfull[s],
+                          a.k_col + hk * a.hsk + at * 64, row_base + (kb_lo + i) * BK + bx * 64);
           nk = i + 1;
         }
         if (i >= 1) {
-          const int u = i - 1, s = u & 1;
-          if (!mbar_wait(&vempty[s], ((u >> 1) & 1) ^ 1, a.status, kTimeoutAttention)) {
+          const int u = i - 1, s = u % KST;
+          if (!mbar_wait(&vempty[s], ((u / KST) & 1) ^ 1, a.status, kTimeoutAttention)) {
             *abort_flag = 1;
             break;
           }
           mbar_arrive_expect_tx(&vfull[s], Sh::KV_BYTES);
           for (int at = 0; at < ATOMS; ++at)
-            tma_load_2d(sV + s * Sh::KV_BYTES + at * (BK * 128), &tmap, &vfull[s], a.v_col + hk * a.hsk + at * 64,
-                        row_base + (kb_lo + u) * BK);
+            for (int bx = 0; bx < BK / 64; ++bx)
+              tma_load_2d(sV + s * Sh::KV_BYTES + at * (BK * 128) + bx * (64 * 128), &tmap, &vfull[s],
+                          a.v_col + hk * a.hsk + at * 64, row_base + (kb_lo + u) * BK + bx * 64);
           nv = u + 1;
         }
       }
-      // Gate prefetch: once the last QK^T has consumed both K stages, load
+      // Gate prefetch: once the last QK^T has consumed every K stage, load
       // this tile's gate rows (128 x D) into them for the epilogue.
       bool gate_issued = false;
       if (a.gate && !*abort_flag && nk == n) {
         bool free_ = true;
-        for (int t = max(0, n - 2); t < n; ++t)
-          free_ = free_ && mbar_wait(&kempty[t & 1], (t >> 1) & 1, a.status, kTimeoutAttention);
+        for (int t = max(0, n - KST); t < n; ++t)
+          free_ = free_ && mbar_wait(&kempty[t % KST], (t / KST) & 1, a.status, kTimeoutAttention);
         if (free_) {
           mbar_arrive_expect_tx(gfull, Sh::Q_BYTES);
           for (int at = 0; at < ATOMS; ++at)
@@ -209,24 +220,24 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
         }
       }
       // Every issued load must land before the CTA may exit (only the last
-      // two per ring can still be in flight: earlier stages were re-awaited).
+      // KST per ring can still be in flight: earlier stages were re-awaited).
       mbar_wait(qfull, 0, a.status, kTimeoutDrain);
       if (gate_issued) mbar_wait(gfull, 0, a.status, kTimeoutDrain);
-      for (int t = max(0, nk - 2); t < nk; ++t) mbar_wait(&kfull[t & 1], (t >> 1) & 1, a.status, kTimeoutDrain);
-      for (int t = max(0, nv - 2); t < nv; ++t) mbar_wait(&vfull[t & 1], (t >> 1) & 1, a.status, kTimeoutDrain);
+      for (int t = max(0, nk - KST); t < nk; ++t) mbar_wait(&kfull[t % KST], (t / KST) & 1, a.status, kTimeoutDrain);
+      for (int t = max(0, nv - KST); t < nv; ++t) mbar_wait(&vfull[t % KST], (t / KST) & 1, a.status, kTimeoutDrain);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       const uint32_t q_addr = smem_u32(sQ);
       auto issue_pv = [&](int u) -> bool {
-        const int s = u & 1;
+        const int s = u & 1, vs = u % KST;  // S/P buffer, V stage
         const uint32_t ph = (u >> 1) & 1;
         if (!mbar_wait(&pfull[s], ph, a.status, kTimeoutAttention) ||
-            !mbar_wait(&vfull[s], ph, a.status, kTimeoutAttention))
+            !mbar_wait(&vfull[vs], (u / KST) & 1, a.status, kTimeoutAttention))
           return false;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + s * Sh::KV_BYTES);
+        const uint32_t v_addr = smem_u32(sV + vs * Sh::KV_BYTES);
         if constexpr (Sh::P_TMEM) {
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)  // 16 keys of P = 8 TMEM columns
@@ -239,29 +250,29 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
             umma_bf16(tmem + Sh::O_COL, smem_desc_k128(p_addr + kk * 32),
                       smem_desc_mn128(v_addr + kk * 16 * 128, BK * 128), IDESC_PV, (u > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&vempty[s]);
+        umma_commit(&vempty[vs]);
         umma_commit(&pempty[s]);
         umma_commit(ofull);
         return true;
       };
       bool ok = mbar_wait(qfull, 0, a.status, kTimeoutAttention);
       for (int t = 0; ok && t < n && !*abort_flag; ++t) {
-        const int s = t & 1;
+        const int s = t & 1, ks = t % KST;  // S buffer, K stage
         const uint32_t ph = (t >> 1) & 1;
-        if (!mbar_wait(&kfull[s], ph, a.status, kTimeoutAttention) ||
+        if (!mbar_wait(&kfull[ks], (t / KST) & 1, a.status, kTimeoutAttention) ||
             !mbar_wait(&sfree[s], ph ^ 1, a.status, kTimeoutAttention)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * Sh::KV_BYTES);
+        const uint32_t k_addr = smem_u32(sK + ks * Sh::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int at = kk >> 2, w = kk & 3;
           umma_bf16(tmem + Sh::S_COL + s * BK, smem_desc_k128(q_addr + at * (BQ * 128) + w * 32),
                     smem_desc_k128(k_addr + at * (BK * 128) + w * 32), IDESC_QK, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&kempty[s]);
+        umma_commit(&kempty[ks]);
         umma_commit(&sfull[s]);
         if (t >= 1 && !issue_pv(t - 1)) {
           ok = false;
@@ -286,10 +297,10 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
     const uint8_t* mrow = a.key_mask ? a.key_mask + static_cast<long long>(b) * a.S : nullptr;
     const bool flags = a.softcap > 0.f || a.window > 0;
     bool ok = true;
-    uint4 mnext[4];  // key-mask bytes of the next tile, in flight while the current one is processed
+    uint4 mnext[BK / 16];  // key-mask bytes of the next tile, in flight while the current one is processed
     auto load_mask = [&](int kk) {
 #pragma unroll
-      for (int v4 = 0; v4 < 4; ++v4)
+      for (int v4 = 0; v4 < BK / 16; ++v4)
         mnext[v4] = (mrow && a.mask_vec && kk + 16 * v4 < a.S) ? *reinterpret_cast<const uint4*>(mrow + kk + 16 * v4)
                                                                  : make_uint4(0, 0, 0, 0);
     };
@@ -305,41 +316,48 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
         break;
       }
       tc_fence_after();
-      uint32_t sr[64];  // the loads run while the key mask below is examined
-      tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      uint32_t sr[BK];  // the loads run while the key mask below is examined
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+        tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK + 32 * w, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * w]));
       // Key validity for this tile (the same for every row): bit c = key k0 + c.
-      uint32_t vbits[2] = {0xffffffffu, 0xffffffffu};
+      uint32_t vbits[NW];
+#pragma unroll
+      for (int w = 0; w < NW; ++w) vbits[w] = 0xffffffffu;
       if (k0 + BK > a.S) {
-        const int nv = a.S - k0;  // 1..63 keys exist
-        vbits[0] = nv >= 32 ? 0xffffffffu : ((1u << nv) - 1u);
-        vbits[1] = nv >= 64 ? 0xffffffffu : (nv <= 32 ? 0u : ((1u << (nv - 32)) - 1u));
+        const int nv = a.S - k0;  // 1..BK-1 keys exist
+#pragma unroll
+        for (int w = 0; w < NW; ++w)
+          vbits[w] = nv >= 32 * (w + 1) ? 0xffffffffu : (nv <= 32 * w ? 0u : ((1u << (nv - 32 * w)) - 1u));
       }
       if (mrow) {
         if (a.mask_vec) {
           // this tile's mask bytes were loaded at the end of the previous tile
           uint32_t all = 0x01010101u;
-          uint4 w[4];
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            w[v4] = mnext[v4];
-            all &= w[v4].x & w[v4].y & w[v4].z & w[v4].w;
-          }
+          for (int v4 = 0; v4 < BK / 16; ++v4) all &= mnext[v4].x & mnext[v4].y & mnext[v4].z & mnext[v4].w;
           if (all != 0x01010101u) {  // some key masked: build the bits (0/1 bytes)
-            uint32_t bits[2] = {0u, 0u};
+            uint32_t bits[NW];
 #pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-              const uint32_t ww[4] = {w[v4].x, w[v4].y, w[v4].z, w[v4].w};
+            for (int w = 0; w < NW; ++w) bits[w] = 0u;
+#pragma unroll
+            for (int v4 = 0; v4 < BK / 16; ++v4) {
+              const uint32_t ww[4] = {mnext[v4].x, mnext[v4].y, mnext[v4].z, mnext[v4].w};
 #pragma unroll
               for (int e = 0; e < 16; ++e)
                 bits[v4 >> 1] |= (((ww[e >> 2] >> (8 * (e & 3))) & 0xffu) != 0u ? 1u : 0u) << (16 * (v4 & 1) + e);
             }
-            vbits[0] &= bits[0];
-            vbits[1] &= bits[1];
+#pragma unroll
+            for (int w = 0; w < NW; ++w) vbits[w] &= bits[w];
           }
         } else {
-          for (int c = 0; c < 64; ++c)
-            if (k0 + c >= a.S || !mrow[k0 + c]) vbits[c >> 5] &= ~(1u << (c & 31));
+#pragma unroll
+          for (int w = 0; w < NW; ++w) {  // word by word: vbits stays in registers
+            uint32_t bw = vbits[w];
+            for (int c = 0; c < 32; ++c)
+              if (k0 + 32 * w + c >= a.S || !mrow[k0 + 32 * w + c]) bw &= ~(1u << c);
+            vbits[w] = bw;
+          }
         }
       }
       tmem_wait_ld();
@@ -350,16 +368,19 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       // in place; a masked entry becomes -1e30 (MASK_FILL semantics: a row
       // with no valid key averages every key).
       const bool diag = k0 + BK - 1 > q0;
-      if (diag || flags || (vbits[0] & vbits[1]) != 0xffffffffu) {
+      uint32_t vall = 0xffffffffu;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) vall &= vbits[w];
+      if (diag || flags || vall != 0xffffffffu) {
         if (a.softcap > 0.f) {  // beyond-reference flag: kept out of the hot loop below
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
+          for (int c = 0; c < BK; ++c)
             sr[c] = __float_as_uint(a.softcap * tanhf(__uint_as_float(sr[c]) * scale / a.softcap) / scale);
         }
         const int lim = row - k0;  // keys k0 + c with c <= lim are not in the future
         const int wlo = a.window > 0 ? row - a.window + 1 - k0 : -1;  // and c >= wlo inside the window
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < BK; ++c) {
           const bool valid = ((vbits[c >> 5] >> (c & 31)) & 1u) && c <= lim && c >= wlo;
           sr[c] = valid ? sr[c] : __float_as_uint(kMaskFill);
         }
@@ -369,7 +390,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) pm[e] = __uint_as_float(sr[e]);
 #pragma unroll
-      for (int c = 8; c < 64; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
+      for (int c = 8; c < BK; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
       const float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       const float mn = fmaxf(m, mt * scale_log2);
       if (t == 0) {
@@ -408,26 +429,25 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
         break;
       }
       if constexpr (Sh::P_TMEM) {
-        uint32_t pw[32];
-        if (m < 0.5f * kMaskFill * scale_log2) {  // every key so far masked: P = 1 (see below)
-          const uint32_t one = pack_bf16x2(1.f, 1.f);
+        // P packed as bf16 pairs over the first BK/2 columns of its S buffer
+        const bool all_masked = m < 0.5f * kMaskFill * scale_log2;  // P = 1 (see below)
+        const float neg_m = -m;
+        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int e = 0; e < 32; ++e) pw[e] = one;
-          l += 64.f;
-        } else {
-          const float neg_m = -m;
-          float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < NW / 2; ++w) {
+          uint32_t pw[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * e]), scale_log2, neg_m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * e + 1]), scale_log2, neg_m));
-            ps[(2 * e) & 7] += p0;
-            ps[(2 * e + 1) & 7] += p1;
+            const int c = 64 * w + 2 * e;
+            const float p0 = all_masked ? 1.f : ex2_approx(fmaf(__uint_as_float(sr[c]), scale_log2, neg_m));
+            const float p1 = all_masked ? 1.f : ex2_approx(fmaf(__uint_as_float(sr[c + 1]), scale_log2, neg_m));
+            ps[c & 7] += p0;
+            ps[(c + 1) & 7] += p1;
             pw[e] = pack_bf16x2(p0, p1);
           }
-          l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+          tmem_st32(tmem + t_lane + Sh::S_COL + s * BK + 32 * w, pw);
         }
-        tmem_st32(tmem + t_lane + Sh::S_COL + s * BK, pw);
+        l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&pfull[s]);
