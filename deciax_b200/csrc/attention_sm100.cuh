@@ -1,6 +1,7 @@
 // Causal GQA flash attention on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA = 128 query rows of one (batch row, query head), 192 threads:
+// One CTA = 128 query rows of one (batch row, query head), 192 threads
+// (320 at head_dim 256, see below):
 //   warp 0      TMA producer: the Q tile once, then K and V in 64-key tiles
 //               through two-stage rings (128-byte swizzle, no multicast).
 //   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M=128, N=64,
@@ -14,11 +15,15 @@
 //               P = exp(s - m) as bf16 into swizzled shared memory for the
 //               P.V MMA, and at the end reads O from TMEM, divides by the sum,
 //               applies the sigmoid output gate and stores.
-// For D = 128 the softmax writes P back into tensor memory over the first 32
-// columns of its own S buffer (bf16 pairs), and the P.V MMA reads A from
-// there.  Without the two shared-memory P buffers the CTA takes 97 KB, so two
-// CTAs share an SM (256 TMEM columns each) and one CTA's softmax overlaps the
-// other's MMAs.  The next QK^T into that S buffer is issued after the P.V
+// For D >= 128 the softmax writes P back into tensor memory over the first
+// BK/2 columns of its own S buffer (bf16 pairs), and the P.V MMA reads A from
+// there.  At D = 128, without the two shared-memory P buffers the CTA takes
+// 97 KB, so two CTAs share an SM (256 TMEM columns each) and one CTA's softmax
+// overlaps the other's MMAs.  At D = 256 one CTA fills the SM: keys come in
+// 128-key tiles (QK^T at N = 128), and warps 2..9 run the softmax, two per
+// row (warps w and w + 4 share a TMEM lane quarter, each taking 64 keys of
+// the tile and half of O's columns), exchanging their tile maxima through
+// shared memory.  The next QK^T into that S buffer is issued after the P.V
 // that reads it, and one thread's tcgen05.mma instructions run in order.
 // The running max is only moved (and O rescaled through TMEM) when it grows
 // by more than 2^8 (log2 units): between moves P is computed against a stale
@@ -61,15 +66,23 @@ struct AttnTcShape {
   static constexpr int BQ = 128, BK = D == 256 ? 128 : 64, ATOMS = D / 64;
   static constexpr int KST = D == 256 ? 1 : 2;         // K and V stages each
   static constexpr bool P_TMEM = D >= 128;             // P over its S buffer in tensor memory
+  // Softmax warps per tensor-memory lane quarter: at head_dim 256 two warps
+  // share each row, one per half of the 128-key tile (one CTA per SM, so the
+  // softmax, which is latency-bound with one warp per scheduler, gets twice
+  // the warps).
+  static constexpr int NP = D == 256 ? 2 : 1;
+  static constexpr int THREADS = 64 + 128 * NP;
+  static constexpr uint32_t XCH_BYTES = NP > 1 ? 3 * NP * 128 * 4 : 0;  // row maxima [2][NP][128], sums [NP][128]
   static constexpr uint32_t Q_BYTES = BQ * D * 2;      // ATOMS x [128 rows x 128 B]
   static constexpr uint32_t KV_BYTES = BK * D * 2;     // ATOMS x [BK rows x 128 B]
   static constexpr uint32_t P_BYTES = BQ * BK * 2;     // [128 rows x 2 BK B]
   static constexpr uint32_t TMEM_COLS = D + 2 * BK <= 256 ? 256 : 512;
   static constexpr uint32_t S_COL = 0, O_COL = 2 * BK;  // S buffers at 0 and BK, O after them
-  static constexpr size_t SMEM = 1024 + Q_BYTES + 2 * KST * KV_BYTES + (P_TMEM ? 0 : 2 * P_BYTES) + 256;
+  static constexpr size_t SMEM = 1024 + Q_BYTES + 2 * KST * KV_BYTES + (P_TMEM ? 0 : 2 * P_BYTES) + 256 + XCH_BYTES;
   static_assert(D + 2 * BK <= 512, "tensor memory");
   static_assert(Q_BYTES <= KST * KV_BYTES, "the gate tile is prefetched into the K stages");
   static_assert(P_TMEM || BK == 64, "P through shared memory is laid out for 64-key tiles");
+  static_assert(NP == 1 || (P_TMEM && (BK / NP) % 64 == 0), "each softmax part writes whole 32-column P chunks");
 };
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -99,8 +112,22 @@ __device__ __forceinline__ uint64_t smem_desc_mn128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// Barrier `id` over `n` threads that also ORs `v` across them (bar.red.or).
+__device__ __forceinline__ bool bar_red_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
+__global__ void __launch_bounds__(AttnTcShape<D>::THREADS, D == 128 ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_out, AttnTcArgs a) {
   using Sh = AttnTcShape<D>;
   constexpr int BQ = Sh::BQ, BK = Sh::BK, ATOMS = Sh::ATOMS, KST = Sh::KST, NW = BK / 32;
@@ -130,6 +157,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
   uint64_t* gfull = bars + 20;  // gate tile prefetched into the K stages
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // softmax parts' exchange
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = (a.S + BQ - 1) / BQ;
@@ -146,7 +174,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
     prefetch_tmap(&tmap);
     for (int i = 0; i < 21; ++i) {
       const bool softmax_arrives = (i >= 11 && i < 15);  // sfree[2], pfull[2]: one arrive per softmax thread
-      mbar_init(&bars[i], softmax_arrives ? 128 : 1);
+      mbar_init(&bars[i], softmax_arrives ? 128 * Sh::NP : 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -287,47 +315,66 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
     }
   } else {
     // ---------------- softmax / epilogue warps ----------------
+    // NP warps per TMEM lane quarter: part p of row r takes keys
+    // [p BKP, (p + 1) BKP) of every tile and O columns [p D/NP, (p + 1) D/NP).
+    // The parts exchange their tile maxima through shared memory (one
+    // barrier per tile); their row sums are added once, at the end.
+    constexpr int NP = Sh::NP, BKP = BK / NP, NWP = BKP / 32, NT = 128 * NP, DP = D / NP;
     const int q4 = warp & 3;  // TMEM lane quarter
+    const int part = (warp - 2) >> 2;
+    const int c0 = part * BKP;  // this part's first key column within a tile
     const int r = q4 * 32 + lane;
     const int row = q0 + r;
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     const float scale = rsqrtf(static_cast<float>(D));
     const float scale_log2 = scale * LOG2E;
-    float m = -INFINITY, l = 0.f;  // running max (log2 units, possibly stale by < 8) and sum
+    float m = -INFINITY, l = 0.f;  // running max (log2 units, possibly stale by < 8) and this part's sum
     const uint8_t* mrow = a.key_mask ? a.key_mask + static_cast<long long>(b) * a.S : nullptr;
     const bool flags = a.softcap > 0.f || a.window > 0;
     bool ok = true;
-    uint4 mnext[BK / 16];  // key-mask bytes of the next tile, in flight while the current one is processed
+    // A failed wait sets `fail`.  With one part a warp leaves the loop at
+    // once; with several, never alone: the next tile's exchange barrier ORs
+    // the flags and every part leaves together.
+    bool fail = false;
+    uint4 mnext[BKP / 16];  // key-mask bytes of the next tile, in flight while the current one is processed
     auto load_mask = [&](int kk) {
 #pragma unroll
-      for (int v4 = 0; v4 < BK / 16; ++v4)
-        mnext[v4] = (mrow && a.mask_vec && kk + 16 * v4 < a.S) ? *reinterpret_cast<const uint4*>(mrow + kk + 16 * v4)
-                                                                 : make_uint4(0, 0, 0, 0);
+      for (int v4 = 0; v4 < BKP / 16; ++v4)
+        mnext[v4] = (mrow && a.mask_vec && kk + c0 + 16 * v4 < a.S)
+                        ? *reinterpret_cast<const uint4*>(mrow + kk + c0 + 16 * v4)
+                        : make_uint4(0, 0, 0, 0);
     };
     load_mask(kb_lo * BK);
     for (int t = 0; t < n; ++t) {
       const int s = t & 1;
       const uint32_t ph = (t >> 1) & 1;
       const int k0 = (kb_lo + t) * BK;
-      const bool ready = mbar_wait(&sfull[s], ph, a.status, kTimeoutAttention);
-      __syncwarp();
-      if (!__all_sync(0xffffffffu, ready)) {
-        ok = false;
-        break;
+      if (!fail) {
+        const bool ready = mbar_wait(&sfull[s], ph, a.status, kTimeoutAttention);
+        __syncwarp();
+        fail = !__all_sync(0xffffffffu, ready);
+      }
+      if constexpr (NP == 1) {
+        if (fail) {
+          ok = false;
+          break;
+        }
       }
       tc_fence_after();
-      uint32_t sr[BK];  // the loads run while the key mask below is examined
+      uint32_t sr[BKP];  // the loads run while the key mask below is examined
+      if (!fail) {
 #pragma unroll
-      for (int w = 0; w < NW; ++w)
-        tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK + 32 * w, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * w]));
-      // Key validity for this tile (the same for every row): bit c = key k0 + c.
-      uint32_t vbits[NW];
+        for (int w = 0; w < NWP; ++w)
+          tmem_ld32(tmem + t_lane + Sh::S_COL + s * BK + c0 + 32 * w, *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * w]));
+      }
+      // Key validity for this part of the tile (the same for every row): bit cc = key k0 + c0 + cc.
+      uint32_t vbits[NWP];
 #pragma unroll
-      for (int w = 0; w < NW; ++w) vbits[w] = 0xffffffffu;
-      if (k0 + BK > a.S) {
-        const int nv = a.S - k0;  // 1..BK-1 keys exist
+      for (int w = 0; w < NWP; ++w) vbits[w] = 0xffffffffu;
+      if (k0 + c0 + BKP > a.S) {
+        const int nv = a.S - k0 - c0;  // keys of this part that exist (may be <= 0)
 #pragma unroll
-        for (int w = 0; w < NW; ++w)
+        for (int w = 0; w < NWP; ++w)
           vbits[w] = nv >= 32 * (w + 1) ? 0xffffffffu : (nv <= 32 * w ? 0u : ((1u << (nv - 32 * w)) - 1u));
       }
       if (mrow) {
@@ -335,34 +382,38 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
           // this tile's mask bytes were loaded at the end of the previous tile
           uint32_t all = 0x01010101u;
 #pragma unroll
-          for (int v4 = 0; v4 < BK / 16; ++v4) all &= mnext[v4].x & mnext[v4].y & mnext[v4].z & mnext[v4].w;
+          for (int v4 = 0; v4 < BKP / 16; ++v4) all &= mnext[v4].x & mnext[v4].y & mnext[v4].z & mnext[v4].w;
           if (all != 0x01010101u) {  // some key masked: build the bits (0/1 bytes)
-            uint32_t bits[NW];
+            uint32_t bits[NWP];
 #pragma unroll
-            for (int w = 0; w < NW; ++w) bits[w] = 0u;
+            for (int w = 0; w < NWP; ++w) bits[w] = 0u;
 #pragma unroll
-            for (int v4 = 0; v4 < BK / 16; ++v4) {
+            for (int v4 = 0; v4 < BKP / 16; ++v4) {
               const uint32_t ww[4] = {mnext[v4].x, mnext[v4].y, mnext[v4].z, mnext[v4].w};
 #pragma unroll
               for (int e = 0; e < 16; ++e)
                 bits[v4 >> 1] |= (((ww[e >> 2] >> (8 * (e & 3))) & 0xffu) != 0u ? 1u : 0u) << (16 * (v4 & 1) + e);
             }
 #pragma unroll
-            for (int w = 0; w < NW; ++w) vbits[w] &= bits[w];
+            for (int w = 0; w < NWP; ++w) vbits[w] &= bits[w];
           }
         } else {
 #pragma unroll
-          for (int w = 0; w < NW; ++w) {  // word by word: vbits stays in registers
+          for (int w = 0; w < NWP; ++w) {  // word by word: vbits stays in registers
             uint32_t bw = vbits[w];
-            for (int c = 0; c < 32; ++c)
-              if (k0 + 32 * w + c >= a.S || !mrow[k0 + 32 * w + c]) bw &= ~(1u << c);
+            for (int c = 0; c < 32; ++c) {
+              const int key = k0 + c0 + 32 * w + c;
+              if (key >= a.S || !mrow[key]) bw &= ~(1u << c);
+            }
             vbits[w] = bw;
           }
         }
       }
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&sfree[s]);
+      if (!fail) {
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sfree[s]);
+      }
       // Raw scores x (= q.k); the softmax uses x * scale_log2.  Boundary tiles
       // (masked keys, the causal diagonal, beyond-reference flags) rewrite x
       // in place; a masked entry becomes -1e30 (MASK_FILL semantics: a row
@@ -370,17 +421,17 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       const bool diag = k0 + BK - 1 > q0;
       uint32_t vall = 0xffffffffu;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) vall &= vbits[w];
+      for (int w = 0; w < NWP; ++w) vall &= vbits[w];
       if (diag || flags || vall != 0xffffffffu) {
         if (a.softcap > 0.f) {  // beyond-reference flag: kept out of the hot loop below
 #pragma unroll
-          for (int c = 0; c < BK; ++c)
+          for (int c = 0; c < BKP; ++c)
             sr[c] = __float_as_uint(a.softcap * tanhf(__uint_as_float(sr[c]) * scale / a.softcap) / scale);
         }
-        const int lim = row - k0;  // keys k0 + c with c <= lim are not in the future
-        const int wlo = a.window > 0 ? row - a.window + 1 - k0 : -1;  // and c >= wlo inside the window
+        const int lim = row - k0 - c0;  // keys k0 + c0 + c with c <= lim are not in the future
+        const int wlo = a.window > 0 ? row - a.window + 1 - k0 - c0 : -BK;  // and c >= wlo inside the window
 #pragma unroll
-        for (int c = 0; c < BK; ++c) {
+        for (int c = 0; c < BKP; ++c) {
           const bool valid = ((vbits[c >> 5] >> (c & 31)) & 1u) && c <= lim && c >= wlo;
           sr[c] = valid ? sr[c] : __float_as_uint(kMaskFill);
         }
@@ -390,27 +441,43 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
 #pragma unroll
       for (int e = 0; e < 8; ++e) pm[e] = __uint_as_float(sr[e]);
 #pragma unroll
-      for (int c = 8; c < BK; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
-      const float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      for (int c = 8; c < BKP; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sr[c]));
+      float mt = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      if constexpr (NP > 1) {
+        // both parts of a row end with the same maximum, bit for bit
+        xbuf[(s * NP + part) * 128 + r] = mt;
+        if (bar_red_or(1, NT, fail)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int p = 0; p < NP; ++p) mt = fmaxf(mt, xbuf[(s * NP + p) * 128 + r]);
+      }
       const float mn = fmaxf(m, mt * scale_log2);
       if (t == 0) {
         m = mn;
       } else {
+        // the parts of a row see the same m and mn, so they decide alike
         const bool need = mn > m + 8.f;
         if (__any_sync(0xffffffffu, need)) {
           // O must hold P_{t-1} V_{t-1} before it is rescaled.
           const bool done = mbar_wait(ofull, (t - 1) & 1, a.status, kTimeoutAttention);
           __syncwarp();
           if (!__all_sync(0xffffffffu, done)) {
-            ok = false;
-            break;
+            fail = true;
+            if constexpr (NP == 1) {
+              ok = false;
+              break;
+            } else {
+              continue;
+            }
           }
           tc_fence_after();
           const float corr = ex2_approx(m - mn);
           m = mn;
           l *= corr;
 #pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
+          for (int c = part * DP; c < (part + 1) * DP; c += 32) {
             uint32_t o[32];
             tmem_ld32(tmem + t_lane + Sh::O_COL + c, o);
             tmem_wait_ld();
@@ -421,20 +488,26 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
           tmem_wait_st();
         }
       }
-      // P = exp2(x * scale_log2 - m) as bf16, row r of the swizzled [128 x 64] tile
+      // P = exp2(x * scale_log2 - m) as bf16
       const bool pe = mbar_wait(&pempty[s], ph ^ 1, a.status, kTimeoutAttention);
       __syncwarp();
       if (!__all_sync(0xffffffffu, pe)) {
-        ok = false;
-        break;
+        fail = true;
+        if constexpr (NP == 1) {
+          ok = false;
+          break;
+        } else {
+          continue;
+        }
       }
       if constexpr (Sh::P_TMEM) {
         // P packed as bf16 pairs over the first BK/2 columns of its S buffer
+        // (key j in column j/2): this part's keys in columns [c0/2, (c0 + BKP)/2)
         const bool all_masked = m < 0.5f * kMaskFill * scale_log2;  // P = 1 (see below)
         const float neg_m = -m;
         float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int w = 0; w < NW / 2; ++w) {
+        for (int w = 0; w < NWP / 2; ++w) {
           uint32_t pw[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
@@ -445,7 +518,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
             ps[(c + 1) & 7] += p1;
             pw[e] = pack_bf16x2(p0, p1);
           }
-          tmem_st32(tmem + t_lane + Sh::S_COL + s * BK + 32 * w, pw);
+          tmem_st32(tmem + t_lane + Sh::S_COL + s * BK + c0 / 2 + 32 * w, pw);
         }
         l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         tmem_wait_st();
@@ -454,45 +527,59 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
         // next tile's mask bytes: loaded after the (release-ordered) arrive, so it does not wait for them
         if (mrow && a.mask_vec) load_mask(k0 + BK);
         continue;
-      }
-      uint8_t* prow = sP + s * Sh::P_BYTES + r * 128;
-      if (m < 0.5f * kMaskFill * scale_log2) {
-        // Every key so far is masked (m is the fill): each entry equals m, so
-        // P = 1 -- the uniform average MASK_FILL gives.  (The FFMA below would
-        // turn the rounding error of the huge product into +-inf here.)
-        const uint32_t one = pack_bf16x2(1.f, 1.f);
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(one, one, one, one);
-        l += 64.f;
       } else {
-        const float neg_m = -m;
-        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
+        // row r of the swizzled [128 x 64] P tile in shared memory (one part)
+        uint8_t* prow = sP + s * Sh::P_BYTES + r * 128;
+        if (m < 0.5f * kMaskFill * scale_log2) {
+          // Every key so far is masked (m is the fill): each entry equals m, so
+          // P = 1 -- the uniform average MASK_FILL gives.  (The FFMA below would
+          // turn the rounding error of the huge product into +-inf here.)
+          const uint32_t one = pack_bf16x2(1.f, 1.f);
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint32_t w[4];
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(one, one, one, one);
+          l += 64.f;
+        } else {
+          const float neg_m = -m;
+          float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e]), scale_log2, neg_m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e + 1]), scale_log2, neg_m));
-            ps[2 * e] += p0;
-            ps[2 * e + 1] += p1;
-            w[e] = pack_bf16x2(p0, p1);
+          for (int ch = 0; ch < 8; ++ch) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e]), scale_log2, neg_m));
+              const float p1 = ex2_approx(fmaf(__uint_as_float(sr[ch * 8 + 2 * e + 1]), scale_log2, neg_m));
+              ps[2 * e] += p0;
+              ps[2 * e + 1] += p1;
+              w[e] = pack_bf16x2(p0, p1);
+            }
+            *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         }
-        l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&pfull[s]);
+        if (mrow && a.mask_vec) load_mask(k0 + BK);  // after the release-ordered arrive (see above)
       }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(&pfull[s]);
-      if (mrow && a.mask_vec) load_mask(k0 + BK);  // after the release-ordered arrive (see above)
     }
+    ok = ok && !fail;
     if (!ok) *abort_flag = 1;
+    if constexpr (NP > 1) {
+      // the row sum: the parts' sums, added in part order
+      float* lbuf = xbuf + 2 * NP * 128;
+      lbuf[part * 128 + r] = l;
+      asm volatile("bar.sync 1, %0;" ::"r"(NT) : "memory");
+      l = 0.f;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) l += lbuf[p * 128 + r];
+    }
     // ---------------- epilogue ----------------
-    // Phase 1: thread r forms its row out = T(T(O / l) * T(sigmoid(gate))) and
-    // writes it into the Q buffer (free: every MMA has completed once ofinal
-    // fires) in the TMA layout [atom][128 rows][128 B] with the 128-byte
-    // swizzle; the gate rows come from the same layout in the K stages.
+    // Phase 1: thread r forms its row out = T(T(O / l) * T(sigmoid(gate))) (its
+    // part's columns) and writes it into the Q buffer (free: every MMA has
+    // completed once ofinal fires) in the TMA layout [atom][128 rows][128 B]
+    // with the 128-byte swizzle; the gate rows come from the same layout in
+    // the K stages.
     const bool fin = ok && mbar_wait(ofinal, 0, a.status, kTimeoutAttention);
     const bool have_gate = fin && a.gate && mbar_wait(gfull, 0, a.status, kTimeoutAttention);
     __syncwarp();
@@ -500,7 +587,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       tc_fence_after();
       const float inv = 1.f / l;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 32) {
+      for (int c = part * DP; c < (part + 1) * DP; c += 32) {
         uint32_t o[32];
         tmem_ld32(tmem + t_lane + Sh::O_COL + c, o);
         tmem_wait_ld();
@@ -537,7 +624,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
       }
     }
     fence_async_smem();  // generic-proxy writes -> visible to the TMA engine
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+    asm volatile("bar.sync 1, %0;" ::"r"(NT) : "memory");  // every softmax warp
     // Phase 2: the tile leaves through TMA bulk stores when it lies inside
     // one sequence; otherwise through coalesced 16-byte stores of its valid rows.
     const int tid = static_cast<int>(threadIdx.x) - 64;
@@ -553,7 +640,7 @@ __global__ void __launch_bounds__(192, D == 128 ? 2 : 1)
     } else {
       constexpr int CPR = D / 8;
 #pragma unroll 4
-      for (int idx = tid; idx < BQ * CPR; idx += 128) {
+      for (int idx = tid; idx < BQ * CPR; idx += NT) {
         const int rr = idx / CPR, ch = idx % CPR;
         if (q0 + rr >= a.S) continue;
         const uint4 ov = *reinterpret_cast<const uint4*>(sQ + (ch >> 3) * (BQ * 128) + rr * 128 + (((ch & 7) ^ (rr & 7)) << 4));

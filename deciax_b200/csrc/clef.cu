@@ -520,7 +520,7 @@ static void attention(Launcher& L, const AttnArgs<T>& a) {
       static std::mutex mu_tc;
       static std::set<std::pair<int, int>> done_tc;
       const int dev = current_device();
-      auto launch = [&](auto kern, size_t smem, int hd) {
+      auto launch = [&](auto kern, size_t smem, int hd, int threads) {
         {
           std::lock_guard<std::mutex> lock(mu_tc);
           if (!done_tc.count({dev, hd})) {
@@ -528,14 +528,14 @@ static void attention(Launcher& L, const AttnArgs<T>& a) {
             done_tc.insert({dev, hd});
           }
         }
-        kern<<<grid, 192, smem, L.stream>>>(map, out_map, t);
+        kern<<<grid, threads, smem, L.stream>>>(map, out_map, t);
       };
       if (a.hd == 64) {
-        launch(attn_tc_kernel<64>, AttnTcShape<64>::SMEM, 64);
+        launch(attn_tc_kernel<64>, AttnTcShape<64>::SMEM, 64, AttnTcShape<64>::THREADS);
       } else if (a.hd == 128) {
-        launch(attn_tc_kernel<128>, AttnTcShape<128>::SMEM, 128);
+        launch(attn_tc_kernel<128>, AttnTcShape<128>::SMEM, 128, AttnTcShape<128>::THREADS);
       } else {
-        launch(attn_tc_kernel<256>, AttnTcShape<256>::SMEM, 256);
+        launch(attn_tc_kernel<256>, AttnTcShape<256>::SMEM, 256, AttnTcShape<256>::THREADS);
       }
       done = true;
     }
