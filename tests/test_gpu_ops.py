@@ -239,11 +239,11 @@ def test_qk_norm_rope(dtype, d, prf):
     np.testing.assert_array_equal(got[..., hq * 2 * d + hkv * d :], qkv[..., hq * 2 * d + hkv * d :])  # v untouched
 
 
-def attention_case(dtype, d, s, softcap=0.0, window=0, lengths=None, seed=0, qscale=1.0):
+def attention_case(dtype, d, s, softcap=0.0, window=0, lengths=None, seed=0, qscale=1.0, hq=4, hkv=2):
     import torch
 
     rng = np.random.default_rng(seed + d + s)
-    b, hq, hkv = 2, 4, 2
+    b = 2
     n = hq * 2 * d + 2 * hkv * d
     qkv = rng.standard_normal((b, s, n)).astype(F32)
     qkv[..., : hq * 2 * d] *= F32(qscale)  # large scores: the running max moves and O is rescaled
@@ -263,6 +263,13 @@ def attention_case(dtype, d, s, softcap=0.0, window=0, lengths=None, seed=0, qsc
     att = O.attention(q, k, v, mask, causal=True, dtype=dtype, flags=flags)
     expected = O.cast(att * O.cast(O.sigmoid(gate), dtype), dtype).reshape(b, s, hq * d)
     return host(out).reshape(b, s, hq * d), expected
+
+
+@pytest.mark.parametrize("hq,hkv", [(2, 2), (8, 2)])
+def test_attention_bf16_d256_group_sizes(hq, hkv):
+    """head_dim 256 with one query head per key/value head and with four."""
+    got, expected = attention_case("bf16", 256, 257, hq=hq, hkv=hkv, seed=7)
+    np.testing.assert_allclose(got, expected, rtol=2e-2, atol=2e-2)
 
 
 @pytest.mark.parametrize("d", [64, 128, 256])
