@@ -1814,7 +1814,8 @@ struct Model {
       const long long r0 = std::min<long long>(Tt, rows_per * rank), r1 = std::min<long long>(Tt, r0 + rows_per);
       a.e0 = r0 * D;
       a.e1 = r1 * D;
-      const long long vecs = (a.e1 - a.e0) / 4;
+      a.vec8 = sizeof(T) == 2 && D % 8 == 0;  // rows of the cudaMalloc'd buffers are then 16-byte aligned
+      const long long vecs = (a.e1 - a.e0) / (a.vec8 ? 8 : 4);
       const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>((vecs + 255) / 256, 148LL * 8)));
       tp_reduce_residual_kernel<T><<<grid, 256, 0, Lc.stream>>>(a);
       CUDA_CHECK(cudaGetLastError());
