@@ -1228,7 +1228,7 @@ def gdn_arm(args) -> None:
                       "flops_per_launch": flops, "frac_of_fp32_cuda_core_peak_at_sampled_clock":
                       (flops / (ms / 1e3) / 1e12 / fp32_peak) if fp32_peak else None,
                       "hbm_bytes_per_launch": moved, "achieved_gbs": moved / (ms / 1e3) / 1e9, "clocks": clk,
-                      "gpu_launches": args.steps}), flush=True)
+                      "gpu_launches": 3 * args.steps}), flush=True)
 
 
 def traffic_per_launch():

@@ -130,7 +130,7 @@ template <int D>
 __global__ void __launch_bounds__(AttnTcShape<D>::THREADS, D == 128 ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap tmap_out, AttnTcArgs a) {
   using Sh = AttnTcShape<D>;
-  constexpr int BQ = Sh::BQ, BK = Sh::BK, ATOMS = Sh::ATOMS, KST = Sh::KST, NW = BK / 32;
+  constexpr int BQ = Sh::BQ, BK = Sh::BK, ATOMS = Sh::ATOMS, KST = Sh::KST;
   constexpr uint32_t IDESC_QK = idesc_bf16_f32(BQ, BK);
   constexpr uint32_t IDESC_PV = idesc_bf16_f32(BQ, D) | (1u << 16);  // B (V) is MN-major
   constexpr float LOG2E = 1.4426950408889634f;

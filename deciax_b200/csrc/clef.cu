@@ -435,19 +435,23 @@ static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
     case 64: launch_gdn_dh<T, 64>(L, a); break;
     case 128:
       if constexpr (sizeof(T) == 2) {
-        // bf16 activations at head dim 128: the tensor-core kernel (TF32 products, FP32 state and solve)
+        // bf16 activations at head dim 128: conv pass, prep pass, chain pass
+        // (tensor cores: TF32 / BF16 products, FP32 state and solve)
         static std::mutex mu;
         static std::set<int> done;
         {
           std::lock_guard<std::mutex> lock(mu);
           if (!done.count(current_device())) {
-            CUDA_CHECK(cudaFuncSetAttribute(gdn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(GdnTcShape::SMEM)));
+            CUDA_CHECK(cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(GdnPrepShape::SMEM)));
+            CUDA_CHECK(cudaFuncSetAttribute(gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(GdnChainShape::SMEM)));
             done.insert(current_device());
           }
         }
-        REQUIRE(a.qkv_conv != nullptr && a.ldc >= static_cast<long long>(2 * a.nh + a.nv) * 128,
-                "the tensor-core Gated DeltaNet path needs the conv-pass buffer");
+        REQUIRE(a.qkv_conv != nullptr && a.prep != nullptr && a.ldc >= static_cast<long long>(2 * a.nh + a.nv) * 128,
+                "the tensor-core Gated DeltaNet path needs its scratch (conv rows and prep records)");
+        REQUIRE(reinterpret_cast<uintptr_t>(a.prep) % 16 == 0, "prep records must be 16-byte aligned");
         const int span = kGdnChunk * kGdnConvBlocks;
         const dim3 cgrid((a.S + span - 1) / span, 2 * a.nh + a.nv, a.B);
         if (a.width <= 4)
@@ -456,7 +460,11 @@ static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
           gdn_conv_bf16_kernel<8><<<cgrid, kGdnThreads, 0, L.stream>>>(a);
         CUDA_CHECK(cudaGetLastError());
         L.tick();
-        gdn_tc_kernel<<<dim3(a.nv, a.B), kGdnThreads, GdnTcShape::SMEM, L.stream>>>(a);
+        const int chunks = (a.S + kGdnChunk - 1) / kGdnChunk;
+        gdn_prep_kernel<<<dim3(chunks, a.nv, a.B), kGdnThreads, GdnPrepShape::SMEM, L.stream>>>(a);
+        CUDA_CHECK(cudaGetLastError());
+        L.tick();
+        gdn_chain_kernel<<<dim3(a.nv, a.B), kGdnThreads, GdnChainShape::SMEM, L.stream>>>(a);
         CUDA_CHECK(cudaGetLastError());
         L.tick();
       } else {
@@ -675,7 +683,7 @@ struct Workspace {
   int b = 0, s = 0, lx = 0, o = 0, q = 0;
   DBuf ints, bytes;  // staged batch arrays (device)
   DBuf x, h, qkv, attn, gu, act, partial, gproj;
-  DBuf gconv;  // Gated DeltaNet conv pass output (bf16, head dim 128): [T, (2 nh_l + nv_l) dh]
+  DBuf gconv;  // Gated DeltaNet tensor-core scratch (bf16, head dim 128): conv rows [T, (2 nh_l + nv_l) dh], prep records
   DBuf tp_flags;  // TP: tile flags of the fused GEMM + reduction (peers write them)
   DBuf memory, mnorm, kv;
   DBuf gv, questions, contexts, lexical;
@@ -1381,7 +1389,7 @@ struct Model {
     grow(w.qkv, act_bytes(T * Nqkv));
     grow(w.attn, act_bytes(T * std::max(Hq_l * d, g_nv_l * g_dh)));
     if (any_linear) grow(w.gproj, act_bytes(T * Ng_pad));
-    if (any_linear && gdn_conv_pass()) grow(w.gconv, T * (2 * g_nh_l + g_nv_l) * g_dh * 2);
+    if (any_linear && gdn_conv_pass()) grow(w.gconv, gdn_tc_scratch_bytes(b, s, g_nh_l, g_nv_l));
     if (dtype == CLEF_DTYPE_F32) grow(w.gu, act_bytes(T * 2 * Fp));
     grow(w.act, act_bytes(T * Fp));
     if (tp > 1) {
@@ -1629,6 +1637,7 @@ struct Model {
     if (gdn_conv_pass()) {
       a.qkv_conv = ws.gconv.p;
       a.ldc = static_cast<long long>(2 * g_nh_l + g_nv_l) * g_dh;
+      a.prep = static_cast<uint8_t*>(ws.gconv.p) + gdn_tc_conv_bytes(bt.b, bt.s, g_nh_l, g_nv_l);
     }
     Lc.cat = kCatGdn;
     launch_gdn<T>(Lc, a, g_dh);
@@ -2507,8 +2516,9 @@ int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int
     if (dtype == CLEF_DTYPE_BF16 && dh == 128) {
       // the conv pass's rows, stream-ordered: allocated and freed on the caller's stream
       a.ldc = static_cast<long long>(2 * nh + nv) * dh;
-      const size_t bytes = static_cast<size_t>(b) * s * a.ldc * 2;
+      const size_t bytes = clef::gdn_tc_scratch_bytes(b, s, nh, nv);
       CUDA_CHECK(cudaMallocFromPoolAsync(&a.qkv_conv, bytes, clef::op_scratch_pool(clef::current_device()), L.stream));
+      a.prep = static_cast<uint8_t*>(a.qkv_conv) + clef::gdn_tc_conv_bytes(b, s, nh, nv);
       try {
         clef::launch_gdn<bf16>(L, a, dh);
       } catch (...) {

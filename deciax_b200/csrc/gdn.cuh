@@ -43,6 +43,8 @@ struct GdnArgs {
   // tensor-core path only: the conv pass's bf16 rows [B*S, ldc] (q heads, k heads, v heads)
   void* qkv_conv;
   long long ldc;
+  // tensor-core path only: the prep pass's per-(chunk, value head, state) records
+  void* prep;
 };
 
 constexpr int kGdnChunk = 64;

@@ -1,42 +1,38 @@
 // Gated DeltaNet mixer core on the 5th-generation tensor cores (sm_100a),
 // BF16 activations, head dim 128: qwen3_5/text.py:48-67 with the chunked rule
-// of kernels/gdn/reference.py:40-92.
+// of kernels/gdn/reference.py:40-92, in three passes over 64-token chunks.
 //
-// One CTA per (state, value head) walks the sequence in 64-token chunks.  The
-// FP32 state S [dk, dv] stays in shared memory in the layout of a tcgen05
-// B operand.  Per chunk (c, c' tokens of the chunk):
-//   L  conv + SiLU, L2 norms and gates as the CUDA-core kernel (gdn.cuh),
-//      written straight into operand layouts: A0 = [k; q] (128 rows), v.
-//   M0 D0 = A0 k^T (M = 128, N = 64, K = 128): rows 0-63 k k^T, rows 64-127 q k^T.
-//   M1 D1 = A0 S (N = 128): rows 0-63 k S, rows 64-127 q S.
-//   P  rows 0-63 of D0 -> the strictly lower system A = -(k beta k^T) * decay;
-//      rows 64-127 -> M = (q k^T) * decay (c' <= c), written back into tensor
-//      memory as the A operand of M3; K~^T = (k e^{g_C - g})^T into tensor
-//      memory (the A operand of M4); R = v - e^g * (k S) in place of v.
-//   T  the inverse T = (I - A)^{-1} (reference.py:73-80) by exact forward
-//      substitution on the CUDA cores, one column per thread, stored as
-//      T diag(beta).
-//   MV V_new = T diag(beta) R (K = 64).  This is reference.py:81-83's
-//      T (v beta) - T (k beta e^g) S, regrouped so that neither product with
-//      T runs over the value and the key dims separately.
-//   M3 D3 = M V_new (A from tensor memory, K = 64).
-//   M4 D2 = K~^T V_new (M = 128, N = 128, K = 64); S = S e^{g_C} + D2
-//      (reference.py:86).
-//   O  rows c: e^{g_c} (q S)_c + D3_c (reference.py:85), then the gated
-//      RMSNorm x SiLU(z) (text.py:61-67).
-// Products run as kind::tf32 (operands rounded to TF32, FP32 accumulation);
-// the inverse, the gates and every elementwise step are FP32.  The FP32
-// parity mode keeps the all-FP32 CUDA-core kernel.
+//   conv   causal conv + SiLU and the q/k L2 norms of every head
+//          (text.py:31-39, reference.py:14-21), bf16 rows [B*S, (2 nh + nv) 128].
+//   prep   per (chunk, value head, state), all in parallel: the gates
+//          g = cumsum(-e^A_log softplus(a + dt_bias)), beta = sigmoid(b)
+//          (text.py:54-55); k k^T and q k^T (tcgen05 kind::f16, exact on the
+//          bf16 values); the system A = -(k beta k^T) * decay and its inverse
+//          T = (I - A)^{-1} (reference.py:73-80, blocked, FP32 on the CUDA
+//          cores); M = (q k^T dk^-1/2) * decay (c' <= c).  Writes one record:
+//          the A operand tile [T diag(beta); M] in the chain's layout and the
+//          gates e^g, e^{g_C - g}.
+//   chain  per (value head, state), the chunks in sequence with the FP32
+//          state S [dk, dv] in shared memory as a tcgen05 B operand:
+//            M1 D1 = [k; q] S;  R = v - e^g (k S);
+//            MV V_new = T diag(beta) R  (reference.py:81-83's
+//               T (v beta) - T (k beta e^g) S, regrouped so that no product
+//               with T runs over the value and the key dims separately);
+//            M3 M V_new;  M4 D2 = K~^T V_new, K~ = k e^{g_C - g};
+//            o = e^g (q S) + M V_new (reference.py:85), S = S e^{g_C} + D2
+//            (reference.py:86), then the gated RMSNorm x SiLU(z)
+//            (text.py:61-67).
+// Products in the chain run as kind::tf32 (operands rounded to TF32, FP32
+// accumulation); the inverse, the gates and every elementwise step are FP32.
+// The FP32 parity mode keeps the all-FP32 CUDA-core kernel (gdn.cuh).
 //
 // Operand tiles are rows of 32 fp32 (128 B) in atoms of `rows` rows per 32
 // columns: a K-major operand [M or N rows][K] with the 128-byte swizzle
 // (16-byte chunks XOR row % 8), an MN-major one [K rows][M or N] with the
 // 128-byte swizzle of 32-byte atomicity (32-byte chunks XOR row % 4), the only
-// swizzle tcgen05 takes for 32-bit MN-major operands.  Tensor memory (512
-// columns): D0 [0, 64), D1 [64, 192), V_new product then D3 [192, 320), D2
-// [320, 448), K~^T [448, 512).  One thread issues the MMAs and commits to one
-// mbarrier; every wait is bounded.  Rows past the sequence end are zero with
-// g = beta = 0, as the reference's padding.
+// swizzle tcgen05 takes for 32-bit MN-major operands.  One thread issues the
+// MMAs and commits to one mbarrier; every wait is bounded.  Rows past the
+// sequence end are zero with g = beta = 0, as the reference's padding.
 #pragma once
 
 #include "attention_sm100.cuh"
@@ -46,20 +42,6 @@
 namespace clef {
 
 constexpr int kGdnTcDim = 128;
-
-struct GdnTcShape {
-  static constexpr int C = kGdnChunk, DH = kGdnTcDim, LDA = C + 4;
-  static constexpr uint32_t S_BYTES = DH * DH * 4;        // state, MN-major B [dk rows][dv]
-  static constexpr uint32_t A0_BYTES = 2 * C * DH * 4;    // [k; q], K-major [128 rows][dk]
-  static constexpr uint32_t V_BYTES = C * DH * 4;         // v -> R -> V_new, MN-major [tokens][dv]
-  static constexpr uint32_t T_BYTES = 2 * C * C * 4;      // T diag(beta), K-major [128 rows][64]; rows 64-127 the unscaled T
-  static constexpr uint32_t AS_BYTES = C * LDA * 4;       // system matrix, row-major
-  static constexpr uint32_t MISC_FLOATS = 4 * C + 2 * C + 32 * 33 + DH;  // gates, norm sums, inverse blocks, norm weight
-  static constexpr int ZLD = DH + 8;  // z rows staged over the system matrix: bf16, 272-byte rows
-  static_assert(C * ZLD * 2 <= AS_BYTES, "z staging");
-  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + AS_BYTES + MISC_FLOATS * 4 + 64;
-  static constexpr uint32_t D0 = 0, D1 = 64, DV = 192, D2 = 320, KT = 448, TMEM_COLS = 512;
-};
 
 // Byte offset of element (row, col) of a K-major fp32 operand tile (rows =
 // M or N, col = K) in atoms of `rows` rows x 32 columns, with the 128-byte
@@ -125,12 +107,12 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-// Stage L as its own pass: causal conv + SiLU (text.py:31-39) of every q, k
-// and v channel and the L2 norms of q and k (reference.py:14-21), written as
-// bf16 rows [B*S, 2*nh*dh + nv*dh] (q heads, k heads, v heads, in projection
-// column order).  Every value is one the reference rounds to bf16, so the
-// chunk kernel reads exactly what it used to compute itself; q leaves without
-// the dk^-1/2 factor.  One CTA per (256-token span, q/k/v head, state): the
+// Conv pass: causal conv + SiLU (text.py:31-39) of every q, k and v channel
+// and the L2 norms of q and k (reference.py:14-21), written as bf16 rows
+// [B*S, 2*nh*dh + nv*dh] (q heads, k heads, v heads, in projection column
+// order).  Every value is one the reference rounds to bf16, so the prep and
+// chain passes read exactly the values the CUDA-core kernel computes in
+// place; q leaves without the dk^-1/2 factor.  One CTA per (256-token span, q/k/v head, state): the
 // q and k heads are computed once, not once per value head that shares them,
 // and the pass runs at full occupancy (each CTA walks kGdnConvBlocks blocks
 // with its taps in registers).  The sliding-window arithmetic is
@@ -196,12 +178,380 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_conv_bf16_kernel(GdnArgs a) {
   }
 }
 
-__global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
-  using Sh = GdnTcShape;
+// ---------------------------------------------------------------------------
+// Prep pass: the state-independent half of every chunk, all chunks at once.
+// ---------------------------------------------------------------------------
+
+// Per (chunk, value head, state): the A operand tile [T diag(beta); M] of the
+// chain kernel's V_new and output products (K-major fp32, 128 rows x 64,
+// the 128-byte swizzle of gdn_sw) and the chunk's gates e^g and e^(g_C - g).
+struct GdnPrepShape {
+  static constexpr int C = kGdnChunk, DH = kGdnTcDim, LDA = C + 4;
+  static constexpr uint32_t TILE_BYTES = 2 * C * C * 4;           // [T diag(beta); M]
+  static constexpr uint32_t GATE_BYTES = 2 * C * 4;               // e^g, e^(g_C - g)
+  static constexpr uint32_t OUT_BYTES = TILE_BYTES + GATE_BYTES;  // per (chunk, value head, state)
+  static constexpr uint32_t A0_BYTES = 2 * C * DH * 2;            // [k; q] bf16, K-major [128 rows][dk];
+                                                                  // after the MMA: system matrix + inverse blocks
+  static constexpr uint32_t TW_BYTES = C * LDA * 4;               // the unscaled inverse, row-major
+  static constexpr uint32_t MISC_FLOATS = 4 * C;                  // gates
+  static_assert(C * LDA * 4 + 32 * 33 * 4 <= A0_BYTES, "system matrix and blocks over the operand tile");
+  static constexpr size_t SMEM = 1024 + A0_BYTES + TW_BYTES + MISC_FLOATS * 4 + 32;
+  static constexpr uint32_t TMEM_COLS = 64;                       // D0 = [k; q] k^T
+  static constexpr int CTAS_PER_SM = 4;
+};
+
+// Byte offset of element (row, col) of a K-major bf16 operand tile in atoms
+// of `rows` rows x 64 columns, with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t gdn_sw16(int row, int col, int rows) {
+  return static_cast<uint32_t>((col >> 6) * (rows * 128) + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) +
+                               ((col & 7) << 1));
+}
+
+// The blocked inverse T = (I - A)^{-1} of a chunk's unit lower-triangular
+// system (reference.py:73-80) into Tw [C][LDA] (zero on entry: blocks above
+// the diagonal are never written).  As [C][LDA] holds A (minus the matrix's
+// off-diagonal).  Diagonal 16 x 16 blocks by forward substitution; then for
+// [[P, 0], [Q, R]] with known inverses P', R' the lower-left block of the
+// inverse is R' (Q~ P'), first for the 16 x 16 pairs of blocks, then for the
+// two 32 x 32 halves.  All threads of the CTA (kGdnThreads) take part.
+__device__ __forceinline__ void gdn_blocked_inverse(float* Tw, const float* As, float* yb, int tid) {
+  constexpr int C = kGdnChunk, LDA = C + 4;
+  auto tw4 = [&](int r, int c4) -> float4 { return *reinterpret_cast<const float4*>(Tw + r * LDA + c4); };
+  if (tid < C) {
+    const int b0 = (tid >> 4) * 16, c = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float* arow = As + (b0 + r) * LDA + b0;
+      float acc0 = r == c ? 1.f : 0.f, acc1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) {
+        if (j & 1)
+          acc1 = fmaf(arow[j], x[j], acc1);
+        else
+          acc0 = fmaf(arow[j], x[j], acc0);
+      }
+      x[r] = acc0 + acc1;
+      Tw[(b0 + r) * LDA + b0 + c] = x[r];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
+    const float* arow = As + (b0b + r) * LDA + a0b;
+    float acc = 0.f;
+#pragma unroll
+    for (int k4 = 0; k4 < 16; k4 += 4) {
+      const float4 a4 = *reinterpret_cast<const float4*>(arow + k4);
+      acc = fmaf(a4.x, Tw[(a0b + k4) * LDA + a0b + c], acc);
+      acc = fmaf(a4.y, Tw[(a0b + k4 + 1) * LDA + a0b + c], acc);
+      acc = fmaf(a4.z, Tw[(a0b + k4 + 2) * LDA + a0b + c], acc);
+      acc = fmaf(a4.w, Tw[(a0b + k4 + 3) * LDA + a0b + c], acc);
+    }
+    yb[m * 16 * 17 + r * 17 + c] = acc;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
+    float acc = 0.f;
+#pragma unroll
+    for (int k4 = 0; k4 < 16; k4 += 4) {
+      const float4 t4 = tw4(b0b + r, b0b + k4);
+      acc = fmaf(t4.x, yb[m * 16 * 17 + k4 * 17 + c], acc);
+      acc = fmaf(t4.y, yb[m * 16 * 17 + (k4 + 1) * 17 + c], acc);
+      acc = fmaf(t4.z, yb[m * 16 * 17 + (k4 + 2) * 17 + c], acc);
+      acc = fmaf(t4.w, yb[m * 16 * 17 + (k4 + 3) * 17 + c], acc);
+    }
+    Tw[(b0b + r) * LDA + a0b + c] = acc;
+  }
+  __syncthreads();
+  {
+    const int c = tid & 31, r0 = tid >> 5;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k4 = 0; k4 < 32; k4 += 4) {
+      float t[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t[e] = Tw[(k4 + e) * LDA + c];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float4 a4 = *reinterpret_cast<const float4*>(As + (32 + r0 + 8 * m) * LDA + k4);
+        acc[m] = fmaf(a4.x, t[0], acc[m]);
+        acc[m] = fmaf(a4.y, t[1], acc[m]);
+        acc[m] = fmaf(a4.z, t[2], acc[m]);
+        acc[m] = fmaf(a4.w, t[3], acc[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) yb[(r0 + 8 * m) * 33 + c] = acc[m];
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < 4; ++m) acc[m] = 0.f;
+#pragma unroll
+    for (int k4 = 0; k4 < 32; k4 += 4) {
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = yb[(k4 + e) * 33 + c];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float4 t4 = tw4(32 + r0 + 8 * m, 32 + k4);
+        acc[m] = fmaf(t4.x, y[0], acc[m]);
+        acc[m] = fmaf(t4.y, y[1], acc[m]);
+        acc[m] = fmaf(t4.z, y[2], acc[m]);
+        acc[m] = fmaf(t4.w, y[3], acc[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) Tw[(32 + r0 + 8 * m) * LDA + c] = acc[m];
+  }
+}
+
+// Untiled bulk copy of `bytes` (a multiple of 16) from this CTA's shared
+// memory to global memory (both 16-byte aligned), in the current bulk group.
+__device__ __forceinline__ void gdn_bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+
+// One CTA per (chunk, value head, state): gates (text.py:54-55: g = -e^A_log
+// softplus(a + dt_bias), beta = sigmoid(b); their in-chunk cumsum), kk^T and
+// qk^T on tcgen05 kind::f16 (q and k are bf16 values, so the products are
+// exact; the dk^-1/2 factor of q is applied after), the system matrix
+// A = -(k beta k^T) * decay (strictly lower), M = (q k^T dk^-1/2) * decay
+// (c' <= c, TF32), and the inverse.  Writes [T diag(beta); M] in the chain
+// kernel's operand layout and the gates e^g, e^(g_C - g).  Four CTAs per SM
+// hide each other's phase latencies.
+__global__ void __launch_bounds__(kGdnThreads, GdnPrepShape::CTAS_PER_SM) gdn_prep_kernel(GdnArgs a) {
+  using Sh = GdnPrepShape;
   using T = __nv_bfloat16;
   constexpr int C = Sh::C, DH = Sh::DH, LDA = Sh::LDA;
-  constexpr uint32_t IDESC_G = idesc_tf32_f32(128, C, false, false);  // A0 k^T: both K-major
-  constexpr uint32_t IDESC_N = idesc_tf32_f32(128, DH, false, true);  // x S, T R, (tmem A) V_new: B MN-major
+  constexpr uint32_t IDESC = idesc_bf16_f32(2 * C, C);  // [k; q] k^T: both K-major
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA0 = smem;
+  float* As = reinterpret_cast<float*>(sA0);  // over the operand tile once the MMA is done: [C][LDA]
+  float* yb = As + C * LDA;                   // [32][33]
+  float* Tw = reinterpret_cast<float*>(sA0 + Sh::A0_BYTES);
+  float* gs = Tw + C * LDA;  // cumulative g
+  float* bs = gs + C;        // beta
+  float* es = bs + C;        // e^g
+  float* ws = es + C;        // e^(g_last - g)
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(ws + C);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+
+  const int ci = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int lrow = quarter * 32 + lane;
+  const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
+  const int hk = h / (a.nv / a.nh), t0 = ci * C;
+  const T* proj = static_cast<const T*>(a.proj);
+  const T* qkv = static_cast<const T*>(a.qkv_conv);
+  const long long row0 = static_cast<long long>(b) * a.S;
+  const float neg_a = -expf(to_f32(static_cast<const T*>(a.A_log)[h]));
+  const float dt_bias = to_f32(static_cast<const T*>(a.dt_bias)[h]);
+  const int chunks = (a.S + C - 1) / C;
+  uint8_t* outp = static_cast<uint8_t*>(a.prep) +
+                  ((static_cast<long long>(b) * a.nv + h) * chunks + ci) * static_cast<long long>(Sh::OUT_BYTES);
+
+  if (tid == 0) {
+    mbar_init(mma_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, Sh::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // gate inputs first (their latency overlaps the tile loads)
+  float ga = 0.f, gb = 0.f;
+  const bool gate_row = tid < C && t0 + tid < a.S;
+  if (gate_row) {
+    const T* pr = proj + (row0 + t0 + tid) * a.ldp;
+    ga = to_f32(pr[a.a_col + h]);
+    gb = to_f32(pr[a.b_col + h]);
+  }
+  // k -> rows 0-63, q -> rows 64-127 of the bf16 operand tile (16-byte copies)
+  {
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + kGdnThreads * i, kind = idx >> 10, r = (idx >> 4) & 63, g8 = (idx & 15) * 8;
+      const int t = t0 + r;
+      v[i] = t < a.S ? *reinterpret_cast<const uint4*>(qkv + (row0 + t) * a.ldc + (kind == 0 ? (a.nh + hk) * DH : hk * DH) + g8)
+                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + kGdnThreads * i, kind = idx >> 10, r = (idx >> 4) & 63, g8 = (idx & 15) * 8;
+      *reinterpret_cast<uint4*>(sA0 + gdn_sw16(kind == 0 ? r : C + r, g8, 2 * C)) = v[i];
+    }
+  }
+  for (int i = tid; i < C * LDA / 4; i += kGdnThreads) reinterpret_cast<float4*>(Tw)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (tid < C) {
+    gs[tid] = gate_row ? neg_a * softplus_f(ga + dt_bias) : 0.f;
+    bs[tid] = gate_row ? round_to<T>(sigmoid_fast(gb)) : 0.f;
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 32) {
+    const uint32_t a0 = smem_u32(sA0);
+#pragma unroll
+    for (int kk = 0; kk < DH / 16; ++kk) {
+      const uint32_t off = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
+      umma_bf16(tmem, smem_desc_k128(a0 + off), smem_desc_k128(a0 + off), IDESC, kk > 0 ? 1u : 0u);
+    }
+    umma_commit(mma_bar);
+  }
+  if (warp == 0) {  // cumulative gate (sequential, as cumsum) and its exponentials
+    if (lane == 0) {
+      float acc = 0.f;
+      for (int r = 0; r < C; ++r) {
+        acc += gs[r];
+        gs[r] = acc;
+      }
+    }
+    __syncwarp();
+    const float last = gs[C - 1];
+    for (int r = lane; r < C; r += 32) {
+      es[r] = expf(gs[r]);
+      ws[r] = expf(last - gs[r]);
+    }
+  }
+  const bool mma_ok = mbar_wait(mma_bar, 0, a.status, kTimeoutMma);
+  tc_fence_after();
+  if (!__syncthreads_and(mma_ok)) {
+    if (warp == 0) tmem_dealloc(tmem, Sh::TMEM_COLS);
+    return;
+  }
+  // system matrix (lanes 0-63, over the operand tile the MMA has read); the
+  // q k^T rows stay in tensor memory until the record is assembled
+  if (lrow < C) {
+    uint32_t d[32];
+    tmem_ld32(tmem + t_lane + 32 * half, d);
+    tmem_wait_ld();
+    const int i = lrow;
+    const float gi = gs[i], bi = bs[i];
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) {
+      float a4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = 32 * half + e + u;
+        a4[u] = j < i ? -(__uint_as_float(d[e + u]) * bi) * exp_fast(gi - gs[j]) : 0.f;
+      }
+      *reinterpret_cast<float4*>(As + i * LDA + 32 * half + e) = make_float4(a4[0], a4[1], a4[2], a4[3]);
+    }
+  }
+  __syncthreads();
+  gdn_blocked_inverse(Tw, As, yb, tid);
+  __syncthreads();
+  // the record in shared memory, over the system matrix: rows 0-63 T diag(beta),
+  // rows 64-127 M = (q k^T dk^-1/2) * decay (c' <= c), both rounded to TF32
+  if (lrow < C) {
+    const int r = lrow;
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) {
+      const int c4 = 32 * half + e;
+      const float4 t4 = *reinterpret_cast<const float4*>(Tw + r * LDA + c4);
+      *reinterpret_cast<float4*>(sA0 + gdn_sw(r, c4, 2 * C)) =
+          make_float4(to_tf32(t4.x * bs[c4]), to_tf32(t4.y * bs[c4 + 1]), to_tf32(t4.z * bs[c4 + 2]),
+                      to_tf32(t4.w * bs[c4 + 3]));
+    }
+  } else {
+    uint32_t d[32];
+    tmem_ld32(tmem + t_lane + 32 * half, d);
+    tmem_wait_ld();
+    const int i = lrow - C;
+    const float gi = gs[i];
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) {
+      float m4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = 32 * half + e + u;
+        m4[u] = j <= i ? to_tf32(__uint_as_float(d[e + u]) * a.qscale * exp_fast(gi - gs[j])) : 0.f;
+      }
+      *reinterpret_cast<float4*>(sA0 + gdn_sw(lrow, 32 * half + e, 2 * C)) = make_float4(m4[0], m4[1], m4[2], m4[3]);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, Sh::TMEM_COLS);
+  if (tid == 0) {  // tile and gates (es, ws adjacent) by two bulk stores
+    gdn_bulk_store(outp, sA0, Sh::TILE_BYTES);
+    gdn_bulk_store(outp + Sh::TILE_BYTES, es, Sh::GATE_BYTES);
+    tma_store_commit();
+    tma_store_wait_read();  // shared memory stays valid until the copies have read it
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chain pass: the state-dependent half of every chunk, in sequence.
+// ---------------------------------------------------------------------------
+
+struct GdnChainShape {
+  static constexpr int C = kGdnChunk, DH = kGdnTcDim;
+  static constexpr uint32_t S_BYTES = DH * DH * 4;        // state, MN-major B [dk rows][dv]
+  static constexpr uint32_t A0_BYTES = 2 * C * DH * 4;    // [k; q dk^-1/2], K-major [128 rows][dk]
+  static constexpr uint32_t V_BYTES = C * DH * 4;         // v -> R -> V_new, MN-major [tokens][dv]
+  static constexpr uint32_t T_BYTES = GdnPrepShape::TILE_BYTES;  // [T diag(beta); M] of the prep pass
+  static constexpr uint32_t G_BYTES = 2 * GdnPrepShape::GATE_BYTES;  // two chunks' gates
+  static constexpr int ZLD = DH + 8;                      // z rows: bf16, 272-byte rows
+  static constexpr uint32_t Z_BYTES = C * ZLD * 2;
+  static constexpr uint32_t MISC_FLOATS = 2 * C + DH;     // output-row sums of squares, norm weight
+  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + G_BYTES + Z_BYTES + MISC_FLOATS * 4 + 64;
+  static constexpr uint32_t D1 = 0, DV = 128, D2 = 256, KT = 384, TMEM_COLS = 512;
+  static_assert(GdnPrepShape::TILE_BYTES % 16 == 0 && GdnPrepShape::GATE_BYTES % 16 == 0 &&
+                    GdnPrepShape::OUT_BYTES % 16 == 0,
+                "bulk copies move 16-byte multiples from 16-byte aligned records");
+};
+
+// Scratch of the tensor-core path for B states of S tokens: the conv pass's
+// bf16 rows [B*S, (2 nh + nv) 128], then (256-byte aligned) the prep pass's
+// records, one of GdnPrepShape::OUT_BYTES per (state, value head, chunk).
+inline size_t gdn_tc_conv_bytes(int B, int S, int nh, int nv) {
+  const size_t bytes = static_cast<size_t>(B) * S * (2 * nh + nv) * kGdnTcDim * 2;
+  return (bytes + 255) & ~size_t(255);
+}
+inline size_t gdn_tc_scratch_bytes(int B, int S, int nh, int nv) {
+  const size_t chunks = (static_cast<size_t>(S) + kGdnChunk - 1) / kGdnChunk;
+  return gdn_tc_conv_bytes(B, S, nh, nv) + static_cast<size_t>(B) * nv * chunks * GdnPrepShape::OUT_BYTES;
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar`
+// (both addresses 16-byte aligned, `bytes` a multiple of 16).
+__device__ __forceinline__ void gdn_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// One CTA per (value head, state) walks the chunks with the FP32 state S in
+// shared memory.  Per chunk: the prep pass's tile [T diag(beta); M] and gates
+// arrive by bulk copy, issued while the previous chunk finishes; q, k and v of
+// the conv pass become TF32 operand tiles (A0 = [k; q dk^-1/2], V);
+//   M1 D1 = A0 S (rows 0-63 k S, rows 64-127 q S);
+//   P  K~^T = (k e^{g_C - g})^T into tensor memory; R = v - e^g (k S) in place of v;
+//   MV D_V = [T diag(beta); M] R: rows 0-63 V_new, stored in place of R;
+//   M3 D_V = [T diag(beta); M] V_new: rows 64-127 M V_new; M4 D2 = K~^T V_new;
+//   O  rows e^g (q S) + M V_new (reference.py:85), gated RMSNorm x SiLU(z);
+//   S = S e^{g_C} + D2 (reference.py:86).
+// Tensor memory: D1 [0, 128), D_V [128, 256), D2 [256, 384), K~^T [384, 448).
+__global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
+  using Sh = GdnChainShape;
+  using T = __nv_bfloat16;
+  constexpr int C = Sh::C, DH = Sh::DH;
+  constexpr uint32_t IDESC_N = idesc_tf32_f32(128, DH, false, true);  // x S, [T; M] R, [T; M] V_new, (tmem A) V_new
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -209,16 +559,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   uint8_t* sA0 = sS + Sh::S_BYTES;
   uint8_t* sV = sA0 + Sh::A0_BYTES;
   uint8_t* sT = sV + Sh::V_BYTES;
-  float* As = reinterpret_cast<float*>(sT + Sh::T_BYTES);  // [C][LDA]
-  float* gs = As + C * LDA;                                // cumulative g
-  float* bs = gs + C;                                      // beta
-  float* es = bs + C;                                      // e^g
-  float* ws = es + C;                                      // e^(g_last - g)
-  float* red = ws + C;                                     // [2][C] output-row partial sums of squares
-  float* yb = red + 2 * C;                                 // [32][33] products of the blocked inverse
-  float* nws = yb + 32 * 33;                               // gated-norm weight
+  float* gates = reinterpret_cast<float*>(sT + Sh::T_BYTES);      // [2][e^g (C), e^(g_C - g) (C)]
+  T* zs = reinterpret_cast<T*>(gates + 4 * C);                    // [C][ZLD]
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(zs) + Sh::Z_BYTES);  // [2][C]
+  float* nws = red + 2 * C;                                       // gated-norm weight
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(nws + DH);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+  uint64_t* tile_bar = mma_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_bar + 1);
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -230,13 +577,15 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   const T* nw = static_cast<const T*>(a.norm_w);
   const T* qkv = static_cast<const T*>(a.qkv_conv);
   T* out = static_cast<T*>(a.out);
-  const float neg_a = -expf(to_f32(static_cast<const T*>(a.A_log)[h]));
-  const float dt_bias = to_f32(static_cast<const T*>(a.dt_bias)[h]);
   const long long row0 = static_cast<long long>(b) * a.S;
   const int q_col = hk * DH, k_col = (a.nh + hk) * DH, v_col = (2 * a.nh + h) * DH;  // columns of the conv pass
+  const int chunks = (a.S + C - 1) / C;
+  const uint8_t* prep = static_cast<const uint8_t*>(a.prep) +
+                        (static_cast<long long>(b) * a.nv + h) * chunks * static_cast<long long>(GdnPrepShape::OUT_BYTES);
 
   if (tid == 0) {
     mbar_init(mma_bar, 1);
+    mbar_init(tile_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -244,14 +593,22 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     tmem_relinquish();
   }
   for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
-  // the T tile starts zero: blocks above the diagonal are never written
-  for (int i = tid; i < 2 * C * C; i += kGdnThreads) reinterpret_cast<float*>(sT)[i] = 0.f;
   if (tid < DH) nws[tid] = to_f32(nw[tid]);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  uint32_t mma_phase = 0;
+  uint32_t mma_phase = 0, tile_phase = 0;
+  bool tile_pending = false;  // thread 0: a tile copy is in flight
+  // chunk ci's record: the tile into sT, the gates into gates[ci & 1]
+  auto load_record = [&](int ci) {
+    const uint8_t* src = prep + static_cast<long long>(ci) * GdnPrepShape::OUT_BYTES;
+    mbar_arrive_expect_tx(tile_bar, GdnPrepShape::OUT_BYTES);
+    gdn_bulk_load(sT, src, GdnPrepShape::TILE_BYTES, tile_bar);
+    gdn_bulk_load(gates + (ci & 1) * 2 * C, src + GdnPrepShape::TILE_BYTES, GdnPrepShape::GATE_BYTES, tile_bar);
+    tile_pending = true;
+  };
+  if (tid == 0) load_record(0);
 
   // One thread issues a group of MMAs and commits; everyone waits for it.
   auto mma_wait = [&]() -> bool {
@@ -262,17 +619,20 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
   };
 
   const uint32_t a0 = smem_u32(sA0), sv = smem_u32(sV), st = smem_u32(sT), ss_addr = smem_u32(sS);
-  const int chunks = (a.S + C - 1) / C;
   for (int ci = 0; ci < chunks; ++ci) {
     const int t0 = ci * C;
-    // ---- L: q, k, v rows of the conv pass into the operand tiles (k -> A0
-    // rows 0-63, q x dk^-1/2 -> A0 rows 64-127, v -> V), and the gates ----
-    float ga = 0.f, gb = 0.f;
-    const bool gate_row = tid < C && t0 + tid < a.S;
-    if (gate_row) {
-      const T* pr = proj + (row0 + t0 + tid) * a.ldp;
-      ga = to_f32(pr[a.a_col + h]);
-      gb = to_f32(pr[a.b_col + h]);
+    const float* es = gates + (ci & 1) * 2 * C;  // e^g
+    const float* ws = es + C;                    // e^(g_last - g)
+    // ---- L: each output thread stages its z row segment (64 bf16) for the
+    // gated norm; q, k, v rows of the conv pass into the operand tiles (k ->
+    // A0 rows 0-63, q x dk^-1/2 -> A0 rows 64-127, v -> V) ----
+    if (lrow >= C) {
+      const int c = lrow - C, t = t0 + c;
+      const T* src = proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + 64 * half;
+      T* dst = zs + c * Sh::ZLD + 64 * half;
+#pragma unroll
+      for (int e8 = 0; e8 < 64; e8 += 8) cp_async16(dst + e8, src + e8, t < a.S);
+      cp_async_commit();
     }
     {
       constexpr int RS = kGdnThreads / 16;  // rows per pass: 16 threads x 8 channels per row
@@ -306,67 +666,34 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
         }
       }
     }
-    if (tid < C) {
-      gs[tid] = gate_row ? neg_a * softplus_f(ga + dt_bias) : 0.f;
-      bs[tid] = gate_row ? round_to<T>(sigmoid_fast(gb)) : 0.f;
-    }
     fence_async_smem();
     __syncthreads();
-    // cumulative gate (sequential, as cumsum) and its exponentials; M0 and M1 meanwhile
-    if (warp == 0) {
-      if (lane == 0) {
-        float acc = 0.f;
-        for (int r = 0; r < C; ++r) {
-          acc += gs[r];
-          gs[r] = acc;
-        }
-      }
-      __syncwarp();
-      const float last = gs[C - 1];
-      for (int r = lane; r < C; r += 32) {
-        es[r] = expf(gs[r]);
-        ws[r] = expf(last - gs[r]);
-      }
-    }
+    // ---- M1: D1 = [k; q] S (the k operand values are exact in TF32: bf16 after the norm) ----
     if (tid == 32) {
-      // ---- M0: D0 = [k; q] k^T;  M1: D1 = [k; q] S (the k operand values
-      // are exact in TF32: bf16 after the norm) ----
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < DH / 8; ++kk) {
         const uint32_t off = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
-        umma_tf32(tmem + Sh::D0, smem_desc_k128(a0 + off), smem_desc_k128(a0 + off), IDESC_G, kk > 0 ? 1u : 0u);
         umma_tf32(tmem + Sh::D1, smem_desc_k128(a0 + off), smem_desc_mn128_32b(ss_addr + kk * 1024, DH * 128),
                   IDESC_N, kk > 0 ? 1u : 0u);
       }
       umma_commit(mma_bar);
     }
-    if (!mma_wait()) break;
-    // ---- P: system matrix (lanes 0-63) or M (lanes 64-127); K~^T; R (lanes 0-63) ----
     {
-      // this thread: tensor-memory lane lrow, D0 columns [32 half, +32)
-      uint32_t d[32];
-      tmem_ld32(tmem + t_lane + Sh::D0 + 32 * half, d);
-      tmem_wait_ld();
-      if (lrow < C) {
-        const int i = lrow;
-        const float gi = gs[i], bi = bs[i];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = 32 * half + e;
-          As[i * LDA + j] = j < i ? -(__uint_as_float(d[e]) * bi) * exp_fast(gi - gs[j]) : 0.f;
-        }
-      } else {
-        const int i = lrow - C;
-        const float gi = gs[i];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int j = 32 * half + e;
-          d[e] = __float_as_uint(j <= i ? to_tf32(__uint_as_float(d[e]) * exp_fast(gi - gs[j])) : 0.f);
-        }
-        tmem_st32(tmem + t_lane + Sh::D0 + 32 * half, d);
+      const bool tile_ok = mbar_wait(tile_bar, tile_phase, a.status, kTimeoutMma);
+      if (tile_ok) {
+        tile_phase ^= 1;
+        if (tid == 0) tile_pending = false;
       }
-      // K~^T: lane (key dim) x columns c in [32 half, +32): k[c][key] e^{g_last - g_c}
+      const bool mma_ok = mbar_wait(mma_bar, mma_phase, a.status, kTimeoutMma);
+      mma_phase ^= 1;
+      tc_fence_after();
+      if (!__syncthreads_and(tile_ok && mma_ok)) break;
+    }
+    // ---- P: K~^T (lane = key dim, columns c in [32 half, +32)) and R = v - e^g (k S)
+    // (lanes 0-63, value dims [64 half, +64)) ----
+    {
+      uint32_t d[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int c = 32 * half + e;
@@ -374,7 +701,6 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       }
       tmem_st32(tmem + t_lane + Sh::KT + 32 * half, d);
       if (lrow < C) {
-        // R = v - e^g (k S), value dims [64 half, +64)
         const int c = lrow;
         const float ec = es[c];
 #pragma unroll
@@ -396,131 +722,10 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       }
       tmem_wait_st();
     }
-    __syncthreads();
-    // ---- T: (I - A)^{-1} by blocks.  The unscaled inverse is built in rows
-    // 64-127 of the T tile (rows the MV product computes but nobody reads);
-    // each block, once final, also goes to rows 0-63 scaled by beta per column
-    // and rounded to TF32: the A operand of MV.  Diagonal 16 x 16 blocks by
-    // forward substitution; then for [[P, 0], [Q, R]] with known inverses P', R'
-    // the lower-left block of the inverse is R' (Q~ P'), Q~ = the system
-    // entries (A holds minus the matrix's off-diagonal), first for the 16 x 16
-    // pairs of blocks, then for the two 32 x 32 halves.  Blocks above the
-    // diagonal are never written and stay zero in both copies. ----
-    {
-      auto tw = [&](int r, int c) -> float& { return *reinterpret_cast<float*>(sT + gdn_sw(C + r, c, 2 * C)); };
-      auto tw4 = [&](int r, int c4) -> float4 {  // working row r, columns c4..c4+3
-        return *reinterpret_cast<const float4*>(sT + gdn_sw(C + r, c4, 2 * C));
-      };
-      auto put = [&](int r, int c, float v) {
-        tw(r, c) = v;
-        *reinterpret_cast<float*>(sT + gdn_sw(r, c, 2 * C)) = to_tf32(v * bs[c]);
-      };
-      if (tid < C) {
-        const int b0 = (tid >> 4) * 16, c = tid & 15;
-        float x[16];
-#pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          const float* arow = As + (b0 + r) * LDA + b0;
-          float acc0 = r == c ? 1.f : 0.f, acc1 = 0.f;
-#pragma unroll
-          for (int j = 0; j < r; ++j) {
-            if (j & 1)
-              acc1 = fmaf(arow[j], x[j], acc1);
-            else
-              acc0 = fmaf(arow[j], x[j], acc0);
-          }
-          x[r] = acc0 + acc1;
-          put(b0 + r, b0 + c, x[r]);
-        }
-      }
-      __syncthreads();
-      // pairs of 16-blocks: Y = A[B0 + r][A0 + k] T[A0 + k][A0 + c]  (T's upper parts are zero)
-#pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
-        const float* arow = As + (b0b + r) * LDA + a0b;
-        float acc = 0.f;
-#pragma unroll
-        for (int k4 = 0; k4 < 16; k4 += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(arow + k4);
-          acc = fmaf(a4.x, tw(a0b + k4, a0b + c), acc);
-          acc = fmaf(a4.y, tw(a0b + k4 + 1, a0b + c), acc);
-          acc = fmaf(a4.z, tw(a0b + k4 + 2, a0b + c), acc);
-          acc = fmaf(a4.w, tw(a0b + k4 + 3, a0b + c), acc);
-        }
-        yb[m * 16 * 17 + r * 17 + c] = acc;
-      }
-      __syncthreads();
-#pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const int a0b = 32 * m, b0b = a0b + 16, r = tid >> 4, c = tid & 15;
-        float acc = 0.f;
-#pragma unroll
-        for (int k4 = 0; k4 < 16; k4 += 4) {
-          const float4 t4 = tw4(b0b + r, b0b + k4);
-          acc = fmaf(t4.x, yb[m * 16 * 17 + k4 * 17 + c], acc);
-          acc = fmaf(t4.y, yb[m * 16 * 17 + (k4 + 1) * 17 + c], acc);
-          acc = fmaf(t4.z, yb[m * 16 * 17 + (k4 + 2) * 17 + c], acc);
-          acc = fmaf(t4.w, yb[m * 16 * 17 + (k4 + 3) * 17 + c], acc);
-        }
-        put(b0b + r, a0b + c, acc);
-      }
-      __syncthreads();
-      // the two halves: Y = A[32 + r][k] T[k][c], then T[32 + r][c] = T[32 + r][32 + k] Y[k][c]
-      {
-        const int c = tid & 31, r0 = tid >> 5;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k4 = 0; k4 < 32; k4 += 4) {
-          float t[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) t[e] = tw(k4 + e, c);
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float4 a4 = *reinterpret_cast<const float4*>(As + (32 + r0 + 8 * m) * LDA + k4);
-            acc[m] = fmaf(a4.x, t[0], acc[m]);
-            acc[m] = fmaf(a4.y, t[1], acc[m]);
-            acc[m] = fmaf(a4.z, t[2], acc[m]);
-            acc[m] = fmaf(a4.w, t[3], acc[m]);
-          }
-        }
-#pragma unroll
-        for (int m = 0; m < 4; ++m) yb[(r0 + 8 * m) * 33 + c] = acc[m];
-        __syncthreads();
-#pragma unroll
-        for (int m = 0; m < 4; ++m) acc[m] = 0.f;
-#pragma unroll
-        for (int k4 = 0; k4 < 32; k4 += 4) {
-          float y[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) y[e] = yb[(k4 + e) * 33 + c];
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float4 t4 = tw4(32 + r0 + 8 * m, 32 + k4);
-            acc[m] = fmaf(t4.x, y[0], acc[m]);
-            acc[m] = fmaf(t4.y, y[1], acc[m]);
-            acc[m] = fmaf(t4.z, y[2], acc[m]);
-            acc[m] = fmaf(t4.w, y[3], acc[m]);
-          }
-        }
-#pragma unroll
-        for (int m = 0; m < 4; ++m) put(32 + r0 + 8 * m, c, acc[m]);
-      }
-    }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // the system matrix is done with: each output thread stages its z row
-    // segment (64 bf16) there for the O phase
-    if (lrow >= C) {
-      const int c = lrow - C, t = t0 + c;
-      const T* src = proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + 64 * half;
-      T* dst = reinterpret_cast<T*>(As) + c * Sh::ZLD + 64 * half;
-#pragma unroll
-      for (int e8 = 0; e8 < 64; e8 += 8) cp_async16(dst + e8, src + e8, t < a.S);
-      cp_async_commit();
-    }
-    // ---- MV: D_V = [T diag(beta); T] R (lanes 64-127 unused) ----
+    // ---- MV: D_V = [T diag(beta); M] R (lanes 0-63: V_new; lanes 64-127 unused) ----
     if (tid == 32) {
       tc_fence_after();
 #pragma unroll
@@ -551,18 +756,31 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    // ---- M3: D3 = M V_new (over the MV product);  M4: D2 = K~^T V_new ----
+    // ---- M3: D_V = [T diag(beta); M] V_new (lanes 64-127: M V_new);  M4: D2 = K~^T V_new ----
     if (tid == 32) {
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < C / 8; ++kk) {
+        const uint32_t aoff = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
         const uint64_t bdesc = smem_desc_mn128_32b(sv + kk * 1024, C * 128);
-        umma_tf32_ts(tmem + Sh::DV, tmem + Sh::D0 + kk * 8, bdesc, IDESC_N, kk > 0 ? 1u : 0u);
+        umma_tf32(tmem + Sh::DV, smem_desc_k128(st + aoff), bdesc, IDESC_N, kk > 0 ? 1u : 0u);
         umma_tf32_ts(tmem + Sh::D2, tmem + Sh::KT + kk * 8, bdesc, IDESC_N, kk > 0 ? 1u : 0u);
       }
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
+    // the tile is read: the next chunk's record comes in while this one finishes
+    if (tid == 0 && ci + 1 < chunks) load_record(ci + 1);
+    // and the next chunk's q, k, v and z rows toward L2 (64 rows x 4 segments of 256 bytes)
+    {
+      const int r = tid >> 2, seg = tid & 3, t = t0 + C + r;
+      if (t < a.S) {
+        const T* src = seg < 3 ? qkv + (row0 + t) * a.ldc + (seg == 0 ? q_col : seg == 1 ? k_col : v_col)
+                               : proj + (row0 + t) * a.ldp + a.z_col + h * DH;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + 64));
+      }
+    }
     // ---- O1 (lanes 64-127): o = T(e^g (q S) + M V_new) into the A0 tile, which
     // no MMA reads any more this chunk (rows of 132 floats), and each row
     // half's sum of squares ----
@@ -624,7 +842,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
       const int c = tid & (C - 1), q32 = (tid >> 6) * 32, t = t0 + c;
       if (t < a.S) {
         const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
-        const T* zrow = reinterpret_cast<const T*>(As) + c * Sh::ZLD + q32;
+        const T* zrow = zs + c * Sh::ZLD + q32;
         const float* orow_s = ob + c * OLD + q32;
         T* orow = out + (row0 + t) * a.ldo + h * DH + q32;
 #pragma unroll
@@ -648,6 +866,10 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_tc_kernel(GdnArgs a) {
     __syncthreads();
   }
 
+  // a tile copy that a failed wait left in flight lands before the CTA's
+  // shared memory is released (bounded: its status is already set)
+  if (tid == 0 && tile_pending) mbar_wait(tile_bar, tile_phase, a.status, kTimeoutMma);
+  cp_async_wait<0>();  // and this thread's z copies
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
