@@ -508,7 +508,7 @@ struct GdnChainShape {
   static constexpr int ZLD = DH + 8;                      // z rows: bf16, 272-byte rows
   static constexpr uint32_t Z_BYTES = C * ZLD * 2;
   static constexpr uint32_t MISC_FLOATS = 2 * C + DH;     // output-row sums of squares, norm weight
-  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + G_BYTES + Z_BYTES + MISC_FLOATS * 4 + 64;
+  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + G_BYTES + Z_BYTES + MISC_FLOATS * 4 + 64;  // + 3 mbarriers, TMEM slot
   static constexpr uint32_t D1 = 0, DV = 128, D2 = 256, KT = 384, TMEM_COLS = 512;
   static_assert(GdnPrepShape::TILE_BYTES % 16 == 0 && GdnPrepShape::GATE_BYTES % 16 == 0 &&
                     GdnPrepShape::OUT_BYTES % 16 == 0,
@@ -536,16 +536,71 @@ __device__ __forceinline__ void gdn_bulk_load(void* dst, const void* src, uint32
                : "memory");
 }
 
+// Stage the q, k, v rows [t0, t0 + C) of the conv pass (bf16) as TF32
+// operand tiles: k -> A0 rows 0-63, q x dk^-1/2 -> A0 rows 64-127 (K-major),
+// v -> V (MN-major).  NTHR threads (lt = 0 .. NTHR-1), 16 per row and 8
+// channels each; rows past the sequence end are zero.
+template <int NTHR, int K0, int K1>  // kinds [K0, K1) of q = 0, k = 1, v = 2
+__device__ __forceinline__ void gdn_stage_rows(uint8_t* sA0, uint8_t* sV, const __nv_bfloat16* rows, int valid,
+                                               long long ldc, int q_col, int k_col, int v_col, float qscale, int lt) {
+  using T = __nv_bfloat16;
+  constexpr int C = kGdnChunk, RS = NTHR / 16, PASSES = 4;  // rows per pass; passes per batch of loads
+  static_assert(C % (RS * PASSES) == 0 && 0 <= K0 && K0 < K1 && K1 <= 3, "row batches, kinds");
+  const int g8 = (lt % 16) * 8;
+#pragma unroll
+  for (int r0 = 0; r0 < C; r0 += RS * PASSES) {
+    uint4 raw[3][PASSES];
+#pragma unroll
+    for (int i = 0; i < PASSES; ++i) {
+      const int r = r0 + lt / 16 + RS * i;
+      const T* src = rows + r * ldc + g8;
+#pragma unroll
+      for (int kind = K0; kind < K1; ++kind)
+        raw[kind][i] = r < valid ? *reinterpret_cast<const uint4*>(src + (kind == 0 ? q_col : kind == 1 ? k_col : v_col))
+                                 : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < PASSES; ++i) {
+      const int r = r0 + lt / 16 + RS * i;
+#pragma unroll
+      for (int kind = K0; kind < K1; ++kind) {
+        const T* hv = reinterpret_cast<const T*>(&raw[kind][i]);
+        float y[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) y[c] = kind == 0 ? to_tf32(__bfloat162float(hv[c]) * qscale) : __bfloat162float(hv[c]);
+#pragma unroll
+        for (int c = 0; c < 8; c += 4) {
+          const float4 v4 = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
+          if (kind == 2)
+            *reinterpret_cast<float4*>(sV + gdn_sw_mn(r, g8 + c, C)) = v4;
+          else
+            *reinterpret_cast<float4*>(sA0 + gdn_sw(kind == 0 ? C + r : r, g8 + c, 2 * C)) = v4;
+        }
+      }
+    }
+  }
+}
+
+// Output row staging over the (read) operand tile: row c, columns j, 128
+// floats per row with 16-byte chunks XOR-permuted by c % 32 (a warp's 32 rows
+// at one column fall in distinct chunks).
+__device__ __forceinline__ int gdn_ob(int c, int j) { return c * 128 + (((j >> 2) ^ (c & 31)) << 2) + (j & 3); }
+
 // One CTA per (value head, state) walks the chunks with the FP32 state S in
-// shared memory.  Per chunk: the prep pass's tile [T diag(beta); M] and gates
-// arrive by bulk copy, issued while the previous chunk finishes; q, k and v of
-// the conv pass become TF32 operand tiles (A0 = [k; q dk^-1/2], V);
+// shared memory.  Per chunk: the prep pass's gates and tile [T diag(beta); M]
+// arrive by bulk copy (the gates while the previous chunk finishes, the tile
+// once its output rows are read); q, k, v were staged as TF32 operand tiles
+// during the previous chunk's output phase (A0 = [k; q dk^-1/2], V);
 //   M1 D1 = A0 S (rows 0-63 k S, rows 64-127 q S);
 //   P  K~^T = (k e^{g_C - g})^T into tensor memory; R = v - e^g (k S) in place of v;
 //   MV D_V = [T diag(beta); M] R: rows 0-63 V_new, stored in place of R;
 //   M3 D_V = [T diag(beta); M] V_new: rows 64-127 M V_new; M4 D2 = K~^T V_new;
-//   O  rows e^g (q S) + M V_new (reference.py:85), gated RMSNorm x SiLU(z);
-//   S = S e^{g_C} + D2 (reference.py:86).
+//   O  lanes 64-127 (warps 2, 3, 6, 7): rows e^g (q S) + M V_new
+//      (reference.py:85) over the tile, S = S e^{g_C} + D2 (reference.py:86)
+//      on their lanes, the next chunk's v tile; lanes 0-63 (warps 0, 1, 4,
+//      5): the state update on theirs, the next chunk's q and k tiles; then
+//      the next chunk's M1 is issued and all warps apply the gated RMSNorm x
+//      SiLU(z) (text.py:61-67) while it runs.
 // Tensor memory: D1 [0, 128), D_V [128, 256), D2 [256, 384), K~^T [384, 448).
 __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   using Sh = GdnChainShape;
@@ -559,13 +614,16 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   uint8_t* sA0 = sS + Sh::S_BYTES;
   uint8_t* sV = sA0 + Sh::A0_BYTES;
   uint8_t* sT = sV + Sh::V_BYTES;
+  float* ob = reinterpret_cast<float*>(sT);                       // output rows, once the tile is read
   float* gates = reinterpret_cast<float*>(sT + Sh::T_BYTES);      // [2][e^g (C), e^(g_C - g) (C)]
   T* zs = reinterpret_cast<T*>(gates + 4 * C);                    // [C][ZLD]
   float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(zs) + Sh::Z_BYTES);  // [2][C]
   float* nws = red + 2 * C;                                       // gated-norm weight
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(nws + DH);
   uint64_t* tile_bar = mma_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_bar + 1);
+  uint64_t* gate_bar = tile_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gate_bar + 1);
+  static_assert(C * 128 * 4 <= Sh::T_BYTES, "output rows over the tile");
 
   const int h = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -586,6 +644,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   if (tid == 0) {
     mbar_init(mma_bar, 1);
     mbar_init(tile_bar, 1);
+    mbar_init(gate_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -594,21 +653,31 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   }
   for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
   if (tid < DH) nws[tid] = to_f32(nw[tid]);
+  gdn_stage_rows<kGdnThreads, 0, 3>(sA0, sV, qkv + row0 * a.ldc, a.S, a.ldc, q_col, k_col, v_col, a.qscale, tid);
+  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  uint32_t mma_phase = 0, tile_phase = 0;
-  bool tile_pending = false;  // thread 0: a tile copy is in flight
+  uint32_t mma_phase = 0, tile_phase = 0, gate_phase = 0;
+  bool tile_pending = false, gate_pending = false;  // thread 0: a copy is in flight
   // chunk ci's record: the tile into sT, the gates into gates[ci & 1]
-  auto load_record = [&](int ci) {
-    const uint8_t* src = prep + static_cast<long long>(ci) * GdnPrepShape::OUT_BYTES;
-    mbar_arrive_expect_tx(tile_bar, GdnPrepShape::OUT_BYTES);
-    gdn_bulk_load(sT, src, GdnPrepShape::TILE_BYTES, tile_bar);
-    gdn_bulk_load(gates + (ci & 1) * 2 * C, src + GdnPrepShape::TILE_BYTES, GdnPrepShape::GATE_BYTES, tile_bar);
+  auto load_tile = [&](int ci) {
+    mbar_arrive_expect_tx(tile_bar, GdnPrepShape::TILE_BYTES);
+    gdn_bulk_load(sT, prep + static_cast<long long>(ci) * GdnPrepShape::OUT_BYTES, GdnPrepShape::TILE_BYTES, tile_bar);
     tile_pending = true;
   };
-  if (tid == 0) load_record(0);
+  auto load_gates = [&](int ci) {
+    mbar_arrive_expect_tx(gate_bar, GdnPrepShape::GATE_BYTES);
+    gdn_bulk_load(gates + (ci & 1) * 2 * C,
+                  prep + static_cast<long long>(ci) * GdnPrepShape::OUT_BYTES + GdnPrepShape::TILE_BYTES,
+                  GdnPrepShape::GATE_BYTES, gate_bar);
+    gate_pending = true;
+  };
+  if (tid == 0) {
+    load_gates(0);
+    load_tile(0);
+  }
 
   // One thread issues a group of MMAs and commits; everyone waits for it.
   auto mma_wait = [&]() -> bool {
@@ -617,15 +686,36 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     tc_fence_after();
     return __syncthreads_and(ok) != 0;
   };
+  // A bulk copy's wait: every thread sees its bytes; thread 0 tracks what is in flight.
+  auto copy_wait = [&](uint64_t* bar, uint32_t& phase, bool& pending) -> bool {
+    const bool ok = mbar_wait(bar, phase, a.status, kTimeoutMma);
+    if (ok) {
+      phase ^= 1;
+      if (tid == 0) pending = false;
+    }
+    return ok;
+  };
 
   const uint32_t a0 = smem_u32(sA0), sv = smem_u32(sV), st = smem_u32(sT), ss_addr = smem_u32(sS);
+  // ---- M1: D1 = [k; q] S (the k operand values are exact in TF32: bf16 after
+  // the norm), issued as soon as a chunk's rows are staged and S is updated ----
+  auto issue_m1 = [&]() {
+#pragma unroll
+    for (int kk = 0; kk < DH / 8; ++kk) {
+      const uint32_t off = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
+      umma_tf32(tmem + Sh::D1, smem_desc_k128(a0 + off), smem_desc_mn128_32b(ss_addr + kk * 1024, DH * 128), IDESC_N,
+                kk > 0 ? 1u : 0u);
+    }
+    umma_commit(mma_bar);
+  };
+  if (tid == 32) issue_m1();
   for (int ci = 0; ci < chunks; ++ci) {
     const int t0 = ci * C;
     const float* es = gates + (ci & 1) * 2 * C;  // e^g
     const float* ws = es + C;                    // e^(g_last - g)
-    // ---- L: each output thread stages its z row segment (64 bf16) for the
-    // gated norm; q, k, v rows of the conv pass into the operand tiles (k ->
-    // A0 rows 0-63, q x dk^-1/2 -> A0 rows 64-127, v -> V) ----
+    // each output thread stages its z row segment (64 bf16) for the gated norm;
+    // the next chunk's rows head for L2 (64 rows x 4 segments of 256 bytes)
+    // while M1 runs
     if (lrow >= C) {
       const int c = lrow - C, t = t0 + c;
       const T* src = proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + 64 * half;
@@ -635,60 +725,20 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       cp_async_commit();
     }
     {
-      constexpr int RS = kGdnThreads / 16;  // rows per pass: 16 threads x 8 channels per row
-      uint4 raw[3][C / RS];
-#pragma unroll
-      for (int i = 0; i < C / RS; ++i) {
-        const int r = tid / 16 + RS * i, t = t0 + r, g8 = (tid % 16) * 8;
-        const T* src = qkv + (row0 + t) * a.ldc + g8;
-#pragma unroll
-        for (int kind = 0; kind < 3; ++kind)
-          raw[kind][i] = t < a.S ? *reinterpret_cast<const uint4*>(src + (kind == 0 ? q_col : kind == 1 ? k_col : v_col))
-                                 : make_uint4(0u, 0u, 0u, 0u);
+      const int r = tid >> 2, seg = tid & 3, t = t0 + C + r;
+      if (t < a.S) {
+        const T* src = seg < 3 ? qkv + (row0 + t) * a.ldc + (seg == 0 ? q_col : seg == 1 ? k_col : v_col)
+                               : proj + (row0 + t) * a.ldp + a.z_col + h * DH;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + 64));
       }
-#pragma unroll
-      for (int i = 0; i < C / RS; ++i) {
-        const int r = tid / 16 + RS * i, g8 = (tid % 16) * 8;
-#pragma unroll
-        for (int kind = 0; kind < 3; ++kind) {
-          const T* hv = reinterpret_cast<const T*>(&raw[kind][i]);
-          float y[8];
-#pragma unroll
-          for (int c = 0; c < 8; ++c) y[c] = kind == 0 ? to_tf32(__bfloat162float(hv[c]) * a.qscale) : __bfloat162float(hv[c]);
-#pragma unroll
-          for (int c = 0; c < 8; c += 4) {
-            const float4 v4 = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
-            if (kind == 2)
-              *reinterpret_cast<float4*>(sV + gdn_sw_mn(r, g8 + c, C)) = v4;
-            else
-              *reinterpret_cast<float4*>(sA0 + gdn_sw(kind == 0 ? C + r : r, g8 + c, 2 * C)) = v4;
-          }
-        }
-      }
-    }
-    fence_async_smem();
-    __syncthreads();
-    // ---- M1: D1 = [k; q] S (the k operand values are exact in TF32: bf16 after the norm) ----
-    if (tid == 32) {
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < DH / 8; ++kk) {
-        const uint32_t off = (kk >> 2) * (2 * C * 128) + (kk & 3) * 32;
-        umma_tf32(tmem + Sh::D1, smem_desc_k128(a0 + off), smem_desc_mn128_32b(ss_addr + kk * 1024, DH * 128),
-                  IDESC_N, kk > 0 ? 1u : 0u);
-      }
-      umma_commit(mma_bar);
     }
     {
-      const bool tile_ok = mbar_wait(tile_bar, tile_phase, a.status, kTimeoutMma);
-      if (tile_ok) {
-        tile_phase ^= 1;
-        if (tid == 0) tile_pending = false;
-      }
+      const bool gate_ok = copy_wait(gate_bar, gate_phase, gate_pending);
       const bool mma_ok = mbar_wait(mma_bar, mma_phase, a.status, kTimeoutMma);
       mma_phase ^= 1;
       tc_fence_after();
-      if (!__syncthreads_and(tile_ok && mma_ok)) break;
+      if (!__syncthreads_and(gate_ok && mma_ok)) break;
     }
     // ---- P: K~^T (lane = key dim, columns c in [32 half, +32)) and R = v - e^g (k S)
     // (lanes 0-63, value dims [64 half, +64)) ----
@@ -724,7 +774,10 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     }
     fence_async_smem();
     tc_fence_before();
-    __syncthreads();
+    {
+      const bool tile_ok = copy_wait(tile_bar, tile_phase, tile_pending);
+      if (!__syncthreads_and(tile_ok)) break;
+    }
     // ---- MV: D_V = [T diag(beta); M] R (lanes 0-63: V_new; lanes 64-127 unused) ----
     if (tid == 32) {
       tc_fence_after();
@@ -769,24 +822,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
-    // the tile is read: the next chunk's record comes in while this one finishes
-    if (tid == 0 && ci + 1 < chunks) load_record(ci + 1);
-    // and the next chunk's q, k, v and z rows toward L2 (64 rows x 4 segments of 256 bytes)
-    {
-      const int r = tid >> 2, seg = tid & 3, t = t0 + C + r;
-      if (t < a.S) {
-        const T* src = seg < 3 ? qkv + (row0 + t) * a.ldc + (seg == 0 ? q_col : seg == 1 ? k_col : v_col)
-                               : proj + (row0 + t) * a.ldp + a.z_col + h * DH;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + 64));
-      }
-    }
-    // ---- O1 (lanes 64-127): o = T(e^g (q S) + M V_new) into the A0 tile, which
-    // no MMA reads any more this chunk (rows of 132 floats), and each row
-    // half's sum of squares ----
-    constexpr int OLD = DH + 4;
-    float* ob = reinterpret_cast<float*>(sA0);
+    // every operand tile is read: the next chunk's gates come in now, its tile
+    // once the output rows (over the tile) are read
+    if (tid == 0 && ci + 1 < chunks) load_gates(ci + 1);
+    const float decay = es[C - 1];
     if (lrow >= C) {
+      // ---- O1 (lanes 64-127): o = T(e^g (q S) + M V_new) into the output
+      // rows, and each row half's sum of squares ----
       const int c = lrow - C;
       const float ec = es[c];
       float sq[4] = {0.f, 0.f, 0.f, 0.f};
@@ -808,34 +850,45 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
           sq[1] = fmaf(o4.y, o4.y, sq[1]);
           sq[2] = fmaf(o4.z, o4.z, sq[2]);
           sq[3] = fmaf(o4.w, o4.w, sq[3]);
-          *reinterpret_cast<float4*>(ob + c * OLD + j0 + e) = o4;
+          *reinterpret_cast<float4*>(ob + gdn_ob(c, j0 + e)) = o4;
         }
       }
       red[half * C + c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
       cp_async_wait<0>();  // this thread's z copies, read by others after the barrier
     }
     // ---- S = S e^{g_last} + D2 (lane = key dim, 64 value columns per thread) ----
-    {
-      const float decay = es[C - 1];
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        uint32_t d[32];
-        const int j0 = 64 * half + 32 * part;
-        tmem_ld32(tmem + t_lane + Sh::D2 + j0, d);
-        tmem_wait_ld();
+    for (int part = 0; part < 2; ++part) {
+      uint32_t d[32];
+      const int j0 = 64 * half + 32 * part;
+      tmem_ld32(tmem + t_lane + Sh::D2 + j0, d);
+      tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          float4* p = reinterpret_cast<float4*>(sS + gdn_sw_mn(lrow, j0 + e, DH));
-          float4 s = *p;
-          s.x = to_tf32(fmaf(s.x, decay, __uint_as_float(d[e])));
-          s.y = to_tf32(fmaf(s.y, decay, __uint_as_float(d[e + 1])));
-          s.z = to_tf32(fmaf(s.z, decay, __uint_as_float(d[e + 2])));
-          s.w = to_tf32(fmaf(s.w, decay, __uint_as_float(d[e + 3])));
-          *p = s;
-        }
+      for (int e = 0; e < 32; e += 4) {
+        float4* p = reinterpret_cast<float4*>(sS + gdn_sw_mn(lrow, j0 + e, DH));
+        float4 s = *p;
+        s.x = to_tf32(fmaf(s.x, decay, __uint_as_float(d[e])));
+        s.y = to_tf32(fmaf(s.y, decay, __uint_as_float(d[e + 1])));
+        s.z = to_tf32(fmaf(s.z, decay, __uint_as_float(d[e + 2])));
+        s.w = to_tf32(fmaf(s.w, decay, __uint_as_float(d[e + 3])));
+        *p = s;
       }
     }
+    // ---- L: the next chunk's rows as operand tiles, q and k by lanes 0-63
+    // (while the others finish the output rows), v by lanes 64-127 ----
+    if (ci + 1 < chunks) {
+      const T* rows = qkv + (row0 + t0 + C) * a.ldc;
+      const int lt = (warp >> 2) * 64 + (quarter & 1) * 32 + lane;
+      if (lrow < C)
+        gdn_stage_rows<kGdnThreads / 2, 0, 2>(sA0, sV, rows, a.S - t0 - C, a.ldc, q_col, k_col, v_col, a.qscale, lt);
+      else
+        gdn_stage_rows<kGdnThreads / 2, 2, 3>(sA0, sV, rows, a.S - t0 - C, a.ldc, q_col, k_col, v_col, a.qscale, lt);
+    }
+    fence_async_smem();
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    if (tid == 32 && ci + 1 < chunks) issue_m1();  // overlaps the gated norm below
     // ---- O2 (all threads, one row per lane, 32 columns per warp quarter of
     // the CTA): gated RMSNorm x SiLU(z) (text.py:61-67) ----
     {
@@ -843,14 +896,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       if (t < a.S) {
         const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
         const T* zrow = zs + c * Sh::ZLD + q32;
-        const float* orow_s = ob + c * OLD + q32;
         T* orow = out + (row0 + t) * a.ldo + h * DH + q32;
 #pragma unroll
         for (int e8 = 0; e8 < 32; e8 += 8) {
           GdnVec<T> z, res;
           z.load(zrow + e8);
-          const float4 o0 = *reinterpret_cast<const float4*>(orow_s + e8);
-          const float4 o1 = *reinterpret_cast<const float4*>(orow_s + e8 + 4);
+          const float4 o0 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, q32 + e8));
+          const float4 o1 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, q32 + e8 + 4));
           const float o[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -864,11 +916,14 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && ci + 1 < chunks) load_tile(ci + 1);
   }
 
-  // a tile copy that a failed wait left in flight lands before the CTA's
-  // shared memory is released (bounded: its status is already set)
+  // copies that a failed wait left in flight land before the CTA's shared
+  // memory is released (bounded: the status is already set)
   if (tid == 0 && tile_pending) mbar_wait(tile_bar, tile_phase, a.status, kTimeoutMma);
+  if (tid == 0 && gate_pending) mbar_wait(gate_bar, gate_phase, a.status, kTimeoutMma);
   cp_async_wait<0>();  // and this thread's z copies
   tc_fence_before();
   __syncthreads();
