@@ -713,17 +713,15 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     const int t0 = ci * C;
     const float* es = gates + (ci & 1) * 2 * C;  // e^g
     const float* ws = es + C;                    // e^(g_last - g)
-    // each output thread stages its z row segment (64 bf16) for the gated norm;
-    // the next chunk's rows head for L2 (64 rows x 4 segments of 256 bytes)
+    // the chunk's z rows for the gated norm (16 threads per 256-byte row), and
+    // the next chunk's rows head for L2 (64 rows x 4 segments of 256 bytes),
     // while M1 runs
-    if (lrow >= C) {
-      const int c = lrow - C, t = t0 + c;
-      const T* src = proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + 64 * half;
-      T* dst = zs + c * Sh::ZLD + 64 * half;
 #pragma unroll
-      for (int e8 = 0; e8 < 64; e8 += 8) cp_async16(dst + e8, src + e8, t < a.S);
-      cp_async_commit();
+    for (int i = 0; i < C * 16 / kGdnThreads; ++i) {
+      const int idx = tid + kGdnThreads * i, c = idx >> 4, e8 = (idx & 15) * 8, t = t0 + c;
+      cp_async16(zs + c * Sh::ZLD + e8, proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + e8, t < a.S);
     }
+    cp_async_commit();
     {
       const int r = tid >> 2, seg = tid & 3, t = t0 + C + r;
       if (t < a.S) {
@@ -854,7 +852,6 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
         }
       }
       red[half * C + c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
-      cp_async_wait<0>();  // this thread's z copies, read by others after the barrier
     }
     // ---- S = S e^{g_last} + D2 (lane = key dim, 64 value columns per thread) ----
 #pragma unroll
@@ -884,6 +881,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       else
         gdn_stage_rows<kGdnThreads / 2, 2, 3>(sA0, sV, rows, a.S - t0 - C, a.ldc, q_col, k_col, v_col, a.qscale, lt);
     }
+    cp_async_wait<0>();  // this thread's z copies, read by others after the barrier
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
