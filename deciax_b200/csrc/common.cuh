@@ -84,6 +84,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// round_to<bf16> of two floats with one paired conversion (cvt.rn.bf16x2.f32:
+// each half rounds to nearest even, the same result as two single roundings).
+__device__ __forceinline__ void round2_bf16(float& a, float& b) {
+  const uint32_t u = pack_bf16x2(a, b);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xFFFF0000u);
+}
+
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }

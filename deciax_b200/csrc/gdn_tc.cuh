@@ -162,16 +162,27 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_conv_bf16_kernel(GdnArgs a) {
         float acc = 0.f;
 #pragma unroll
         for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(x[j + i][c], w[c][i]));
-        const float z = round_to<T>(acc);
-        y.v[c] = t < a.S ? round_to<T>(z * sigmoid_fast(z)) : 0.f;
+        y.v[c] = acc;
       }
+      // bf16 roundings in pairs: z = T(acc), y = T(z sigmoid(z)) (text.py:31-39)
+#pragma unroll
+      for (int c = 0; c < VN; c += 2) round2_bf16(y.v[c], y.v[c + 1]);
+#pragma unroll
+      for (int c = 0; c < VN; ++c) y.v[c] *= sigmoid_fast(y.v[c]);
+#pragma unroll
+      for (int c = 0; c < VN; c += 2) round2_bf16(y.v[c], y.v[c + 1]);
+      if (t >= a.S) y.zero();
       if (kind < 2) {
         float ss = 0.f;
 #pragma unroll
         for (int c = 0; c < VN; ++c) ss += y.v[c] * y.v[c];
         const float inv = rsqrtf(group_sum<GL>(ss) + 1e-6f);
 #pragma unroll
-        for (int c = 0; c < VN; ++c) y.v[c] = round_to<T>(y.v[c] * inv);
+        for (int c = 0; c < VN; c += 2) {
+          y.v[c] *= inv;
+          y.v[c + 1] *= inv;
+          round2_bf16(y.v[c], y.v[c + 1]);
+        }
       }
       if (t < a.S) y.store(dst + (row0 + t) * a.ldc + kh * DH + g * VN);
     }
@@ -840,10 +851,12 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
           float4 o4;
-          o4.x = round_to<T>(fmaf(ec, __uint_as_float(d[e]), __uint_as_float(m[e])));
-          o4.y = round_to<T>(fmaf(ec, __uint_as_float(d[e + 1]), __uint_as_float(m[e + 1])));
-          o4.z = round_to<T>(fmaf(ec, __uint_as_float(d[e + 2]), __uint_as_float(m[e + 2])));
-          o4.w = round_to<T>(fmaf(ec, __uint_as_float(d[e + 3]), __uint_as_float(m[e + 3])));
+          o4.x = fmaf(ec, __uint_as_float(d[e]), __uint_as_float(m[e]));
+          o4.y = fmaf(ec, __uint_as_float(d[e + 1]), __uint_as_float(m[e + 1]));
+          o4.z = fmaf(ec, __uint_as_float(d[e + 2]), __uint_as_float(m[e + 2]));
+          o4.w = fmaf(ec, __uint_as_float(d[e + 3]), __uint_as_float(m[e + 3]));
+          round2_bf16(o4.x, o4.y);
+          round2_bf16(o4.z, o4.w);
           sq[0] = fmaf(o4.x, o4.x, sq[0]);
           sq[1] = fmaf(o4.y, o4.y, sq[1]);
           sq[2] = fmaf(o4.z, o4.z, sq[2]);
@@ -901,12 +914,15 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
           z.load(zrow + e8);
           const float4 o0 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, q32 + e8));
           const float4 o1 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, q32 + e8 + 4));
-          const float o[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+          float n[8] = {o0.x * rs, o0.y * rs, o0.z * rs, o0.w * rs, o1.x * rs, o1.y * rs, o1.z * rs, o1.w * rs};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float n = round_to<T>(round_to<T>(o[e] * rs) * nws[q32 + e8 + e]);
-            res.v[e] = n * (z.v[e] * sigmoid_fast(z.v[e]));
-          }
+          for (int e = 0; e < 8; e += 2) round2_bf16(n[e], n[e + 1]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) n[e] *= nws[q32 + e8 + e];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) round2_bf16(n[e], n[e + 1]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) res.v[e] = n[e] * (z.v[e] * sigmoid_fast(z.v[e]));
           res.store(orow + e8);
         }
       }
