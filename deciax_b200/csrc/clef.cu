@@ -156,6 +156,22 @@ static CUtensorMap tmap_bf16(const void* ptr, uint64_t rows, uint64_t cols, uint
   return m;
 }
 
+// bf16 rows of `states` sequences of `seq` tokens, row stride ld elements, as a
+// [state][token][column] tensor: box 64 columns x box_rows tokens of one state,
+// 128-byte swizzle; tokens past a sequence's end read zero.
+static CUtensorMap tmap_bf16_states(const void* ptr, uint64_t states, uint64_t seq, uint64_t ld, uint32_t box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {ld, seq, states};
+  cuuint64_t strides[2] = {ld * 2, seq * ld * 2};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = tma_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(CLEF_EINVAL, "cuTensorMapEncodeTiled rejected the Gated DeltaNet conv rows");
+  return m;
+}
+
 // ===========================================================================
 // kernel launchers
 // ===========================================================================
@@ -461,7 +477,8 @@ static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
         CUDA_CHECK(cudaGetLastError());
         L.tick();
         const int chunks = (a.S + kGdnChunk - 1) / kGdnChunk;
-        gdn_prep_kernel<<<dim3(chunks, a.nv, a.B), kGdnThreads, GdnPrepShape::SMEM, L.stream>>>(a);
+        const CUtensorMap qk_map = tmap_bf16_states(a.qkv_conv, a.B, a.S, a.ldc, kGdnChunk);
+        gdn_prep_kernel<<<dim3(chunks, a.nh, a.B), kGdnThreads, GdnPrepShape::SMEM, L.stream>>>(qk_map, a);
         CUDA_CHECK(cudaGetLastError());
         L.tick();
         gdn_chain_kernel<<<dim3(a.nv, a.B), kGdnThreads, GdnChainShape::SMEM, L.stream>>>(a);

@@ -206,7 +206,7 @@ struct GdnPrepShape {
   static constexpr uint32_t TW_BYTES = C * LDA * 4;               // the unscaled inverse, row-major
   static constexpr uint32_t MISC_FLOATS = 4 * C;                  // gates
   static_assert(C * LDA * 4 + 32 * 33 * 4 <= A0_BYTES, "system matrix and blocks over the operand tile");
-  static constexpr size_t SMEM = 1024 + A0_BYTES + TW_BYTES + MISC_FLOATS * 4 + 32;
+  static constexpr size_t SMEM = 1024 + A0_BYTES + TW_BYTES + MISC_FLOATS * 4 + 32;  // + 2 mbarriers, TMEM slot
   static constexpr uint32_t TMEM_COLS = 64;                       // D0 = [k; q] k^T
   static constexpr int CTAS_PER_SM = 4;
 };
@@ -327,15 +327,27 @@ __device__ __forceinline__ void gdn_bulk_store(void* dst, const void* src, uint3
                : "memory");
 }
 
-// One CTA per (chunk, value head, state): gates (text.py:54-55: g = -e^A_log
-// softplus(a + dt_bias), beta = sigmoid(b); their in-chunk cumsum), kk^T and
-// qk^T on tcgen05 kind::f16 (q and k are bf16 values, so the products are
-// exact; the dk^-1/2 factor of q is applied after), the system matrix
-// A = -(k beta k^T) * decay (strictly lower), M = (q k^T dk^-1/2) * decay
-// (c' <= c, TF32), and the inverse.  Writes [T diag(beta); M] in the chain
-// kernel's operand layout and the gates e^g, e^(g_C - g).  Four CTAs per SM
-// hide each other's phase latencies.
-__global__ void __launch_bounds__(kGdnThreads, GdnPrepShape::CTAS_PER_SM) gdn_prep_kernel(GdnArgs a) {
+// 3-D tiled load (x = column, y = row, z = state) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// One CTA per (chunk, key head, state), for each value head of the key head's
+// group in turn: gates (text.py:54-55: g = -e^A_log softplus(a + dt_bias),
+// beta = sigmoid(b); their in-chunk cumsum), the system matrix A = -(k beta
+// k^T) * decay (strictly lower), M = (q k^T dk^-1/2) * decay (c' <= c, TF32)
+// and the inverse; writes [T diag(beta); M] in the chain kernel's operand
+// layout and the gates e^g, e^(g_C - g).  k k^T and q k^T are shared by the
+// group: one TMA load of the bf16 [k; q] tile (the conv pass's rows, as a
+// [state][token][column] tensor: tokens past the sequence end read zero) and
+// one tcgen05 kind::f16 product (exact on bf16 values; dk^-1/2 applied after),
+// kept in tensor memory.  Four CTAs per SM hide each other's phase latencies.
+__global__ void __launch_bounds__(kGdnThreads, GdnPrepShape::CTAS_PER_SM)
+    gdn_prep_kernel(const __grid_constant__ CUtensorMap qk_map, GdnArgs a) {
   using Sh = GdnPrepShape;
   using T = __nv_bfloat16;
   constexpr int C = Sh::C, DH = Sh::DH, LDA = Sh::LDA;
@@ -352,66 +364,46 @@ __global__ void __launch_bounds__(kGdnThreads, GdnPrepShape::CTAS_PER_SM) gdn_pr
   float* es = bs + C;        // e^g
   float* ws = es + C;        // e^(g_last - g)
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(ws + C);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+  uint64_t* load_bar = mma_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(load_bar + 1);
 
-  const int ci = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int ci = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, half = warp >> 2;
   const int lrow = quarter * 32 + lane;
   const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
-  const int hk = h / (a.nv / a.nh), t0 = ci * C;
+  const int group = a.nv / a.nh, t0 = ci * C;
   const T* proj = static_cast<const T*>(a.proj);
-  const T* qkv = static_cast<const T*>(a.qkv_conv);
   const long long row0 = static_cast<long long>(b) * a.S;
-  const float neg_a = -expf(to_f32(static_cast<const T*>(a.A_log)[h]));
-  const float dt_bias = to_f32(static_cast<const T*>(a.dt_bias)[h]);
   const int chunks = (a.S + C - 1) / C;
-  uint8_t* outp = static_cast<uint8_t*>(a.prep) +
-                  ((static_cast<long long>(b) * a.nv + h) * chunks + ci) * static_cast<long long>(Sh::OUT_BYTES);
 
   if (tid == 0) {
     mbar_init(mma_bar, 1);
+    mbar_init(load_bar, 1);
     fence_barrier_init();
+    prefetch_tmap(&qk_map);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, Sh::TMEM_COLS);
     tmem_relinquish();
   }
-  // gate inputs first (their latency overlaps the tile loads)
-  float ga = 0.f, gb = 0.f;
-  const bool gate_row = tid < C && t0 + tid < a.S;
-  if (gate_row) {
-    const T* pr = proj + (row0 + t0 + tid) * a.ldp;
-    ga = to_f32(pr[a.a_col + h]);
-    gb = to_f32(pr[a.b_col + h]);
-  }
-  // k -> rows 0-63, q -> rows 64-127 of the bf16 operand tile (16-byte copies)
-  {
-    uint4 v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int idx = tid + kGdnThreads * i, kind = idx >> 10, r = (idx >> 4) & 63, g8 = (idx & 15) * 8;
-      const int t = t0 + r;
-      v[i] = t < a.S ? *reinterpret_cast<const uint4*>(qkv + (row0 + t) * a.ldc + (kind == 0 ? (a.nh + hk) * DH : hk * DH) + g8)
-                     : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int idx = tid + kGdnThreads * i, kind = idx >> 10, r = (idx >> 4) & 63, g8 = (idx & 15) * 8;
-      *reinterpret_cast<uint4*>(sA0 + gdn_sw16(kind == 0 ? r : C + r, g8, 2 * C)) = v[i];
-    }
-  }
-  for (int i = tid; i < C * LDA / 4; i += kGdnThreads) reinterpret_cast<float4*>(Tw)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (tid < C) {
-    gs[tid] = gate_row ? neg_a * softplus_f(ga + dt_bias) : 0.f;
-    bs[tid] = gate_row ? round_to<T>(sigmoid_fast(gb)) : 0.f;
-  }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 32) {
+  if (tid == 0) {  // k -> rows 0-63, q -> rows 64-127 of each 64-column atom
+    mbar_arrive_expect_tx(load_bar, Sh::A0_BYTES);
+#pragma unroll
+    for (int atom = 0; atom < DH / 64; ++atom) {
+      uint8_t* dst = sA0 + atom * (2 * C * 128);
+      tma_load_3d(dst, &qk_map, load_bar, (a.nh + hk) * DH + 64 * atom, t0, b);
+      tma_load_3d(dst + C * 128, &qk_map, load_bar, hk * DH + 64 * atom, t0, b);
+    }
+  }
+  const bool load_ok = mbar_wait(load_bar, 0, a.status, kTimeoutMma);
+  const bool loaded = __syncthreads_and(load_ok) != 0;
+  if (loaded && tid == 32) {
+    tc_fence_after();
     const uint32_t a0 = smem_u32(sA0);
 #pragma unroll
     for (int kk = 0; kk < DH / 16; ++kk) {
@@ -420,89 +412,117 @@ __global__ void __launch_bounds__(kGdnThreads, GdnPrepShape::CTAS_PER_SM) gdn_pr
     }
     umma_commit(mma_bar);
   }
-  if (warp == 0) {  // cumulative gate (sequential, as cumsum) and its exponentials
-    if (lane == 0) {
-      float acc = 0.f;
-      for (int r = 0; r < C; ++r) {
-        acc += gs[r];
-        gs[r] = acc;
-      }
-    }
-    __syncwarp();
-    const float last = gs[C - 1];
-    for (int r = lane; r < C; r += 32) {
-      es[r] = expf(gs[r]);
-      ws[r] = expf(last - gs[r]);
-    }
-  }
-  const bool mma_ok = mbar_wait(mma_bar, 0, a.status, kTimeoutMma);
+  const bool ok = loaded && mbar_wait(mma_bar, 0, a.status, kTimeoutMma);
   tc_fence_after();
-  if (!__syncthreads_and(mma_ok)) {
+  if (!__syncthreads_and(ok)) {
+    // a load that a failed wait left in flight lands before shared memory is
+    // released (bounded: the status is already set)
+    if (tid == 0 && !load_ok) mbar_wait(load_bar, 0, a.status, kTimeoutMma);
+    tc_fence_before();
+    __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, Sh::TMEM_COLS);
     return;
   }
-  // system matrix (lanes 0-63, over the operand tile the MMA has read); the
-  // q k^T rows stay in tensor memory until the record is assembled
-  if (lrow < C) {
-    uint32_t d[32];
-    tmem_ld32(tmem + t_lane + 32 * half, d);
-    tmem_wait_ld();
-    const int i = lrow;
-    const float gi = gs[i], bi = bs[i];
-#pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      float a4[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = 32 * half + e + u;
-        a4[u] = j < i ? -(__uint_as_float(d[e + u]) * bi) * exp_fast(gi - gs[j]) : 0.f;
+
+  for (int g = 0; g < group; ++g) {
+    const int h = hk * group + g;
+    uint8_t* outp = static_cast<uint8_t*>(a.prep) +
+                    ((static_cast<long long>(b) * a.nv + h) * chunks + ci) * static_cast<long long>(Sh::OUT_BYTES);
+    if (tid < C) {
+      const bool row = t0 + tid < a.S;
+      float ga = 0.f, gb = 0.f;
+      if (row) {
+        const T* pr = proj + (row0 + t0 + tid) * a.ldp;
+        ga = to_f32(pr[a.a_col + h]);
+        gb = to_f32(pr[a.b_col + h]);
       }
-      *reinterpret_cast<float4*>(As + i * LDA + 32 * half + e) = make_float4(a4[0], a4[1], a4[2], a4[3]);
+      const float neg_a = -expf(to_f32(static_cast<const T*>(a.A_log)[h]));
+      const float dt_bias = to_f32(static_cast<const T*>(a.dt_bias)[h]);
+      gs[tid] = row ? neg_a * softplus_f(ga + dt_bias) : 0.f;
+      bs[tid] = row ? round_to<T>(sigmoid_fast(gb)) : 0.f;
+    }
+    for (int i = tid; i < C * LDA / 4; i += kGdnThreads) reinterpret_cast<float4*>(Tw)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g > 0 && tid == 0) tma_store_wait_read();  // the previous record has left shared memory
+    __syncthreads();
+    if (warp == 0) {  // cumulative gate (sequential, as cumsum) and its exponentials
+      if (lane == 0) {
+        float acc = 0.f;
+        for (int r = 0; r < C; ++r) {
+          acc += gs[r];
+          gs[r] = acc;
+        }
+      }
+      __syncwarp();
+      const float last = gs[C - 1];
+      for (int r = lane; r < C; r += 32) {
+        es[r] = expf(gs[r]);
+        ws[r] = expf(last - gs[r]);
+      }
+    }
+    __syncthreads();
+    // system matrix (lanes 0-63, over the operand tile the MMA has read)
+    if (lrow < C) {
+      uint32_t d[32];
+      tmem_ld32(tmem + t_lane + 32 * half, d);
+      tmem_wait_ld();
+      const int i = lrow;
+      const float gi = gs[i], bi = bs[i];
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float a4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 32 * half + e + u;
+          a4[u] = j < i ? -(__uint_as_float(d[e + u]) * bi) * exp_fast(gi - gs[j]) : 0.f;
+        }
+        *reinterpret_cast<float4*>(As + i * LDA + 32 * half + e) = make_float4(a4[0], a4[1], a4[2], a4[3]);
+      }
+    }
+    __syncthreads();
+    gdn_blocked_inverse(Tw, As, yb, tid);
+    __syncthreads();
+    // the record in shared memory, over the system matrix: rows 0-63 T diag(beta),
+    // rows 64-127 M = (q k^T dk^-1/2) * decay (c' <= c), both rounded to TF32
+    if (lrow < C) {
+      const int r = lrow;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const int c4 = 32 * half + e;
+        const float4 t4 = *reinterpret_cast<const float4*>(Tw + r * LDA + c4);
+        *reinterpret_cast<float4*>(sA0 + gdn_sw(r, c4, 2 * C)) =
+            make_float4(to_tf32(t4.x * bs[c4]), to_tf32(t4.y * bs[c4 + 1]), to_tf32(t4.z * bs[c4 + 2]),
+                        to_tf32(t4.w * bs[c4 + 3]));
+      }
+    } else {
+      uint32_t d[32];
+      tmem_ld32(tmem + t_lane + 32 * half, d);
+      tmem_wait_ld();
+      const int i = lrow - C;
+      const float gi = gs[i];
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float m4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = 32 * half + e + u;
+          m4[u] = j <= i ? to_tf32(__uint_as_float(d[e + u]) * a.qscale * exp_fast(gi - gs[j])) : 0.f;
+        }
+        *reinterpret_cast<float4*>(sA0 + gdn_sw(lrow, 32 * half + e, 2 * C)) = make_float4(m4[0], m4[1], m4[2], m4[3]);
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {  // tile and gates (es, ws adjacent) by two bulk stores
+      gdn_bulk_store(outp, sA0, Sh::TILE_BYTES);
+      gdn_bulk_store(outp + Sh::TILE_BYTES, es, Sh::GATE_BYTES);
+      tma_store_commit();
     }
   }
-  __syncthreads();
-  gdn_blocked_inverse(Tw, As, yb, tid);
-  __syncthreads();
-  // the record in shared memory, over the system matrix: rows 0-63 T diag(beta),
-  // rows 64-127 M = (q k^T dk^-1/2) * decay (c' <= c), both rounded to TF32
-  if (lrow < C) {
-    const int r = lrow;
-#pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      const int c4 = 32 * half + e;
-      const float4 t4 = *reinterpret_cast<const float4*>(Tw + r * LDA + c4);
-      *reinterpret_cast<float4*>(sA0 + gdn_sw(r, c4, 2 * C)) =
-          make_float4(to_tf32(t4.x * bs[c4]), to_tf32(t4.y * bs[c4 + 1]), to_tf32(t4.z * bs[c4 + 2]),
-                      to_tf32(t4.w * bs[c4 + 3]));
-    }
-  } else {
-    uint32_t d[32];
-    tmem_ld32(tmem + t_lane + 32 * half, d);
-    tmem_wait_ld();
-    const int i = lrow - C;
-    const float gi = gs[i];
-#pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      float m4[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = 32 * half + e + u;
-        m4[u] = j <= i ? to_tf32(__uint_as_float(d[e + u]) * a.qscale * exp_fast(gi - gs[j])) : 0.f;
-      }
-      *reinterpret_cast<float4*>(sA0 + gdn_sw(lrow, 32 * half + e, 2 * C)) = make_float4(m4[0], m4[1], m4[2], m4[3]);
-    }
-  }
-  fence_async_smem();
+  if (tid == 0) tma_store_wait_read();  // shared memory stays valid until the copies have read it
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, Sh::TMEM_COLS);
-  if (tid == 0) {  // tile and gates (es, ws adjacent) by two bulk stores
-    gdn_bulk_store(outp, sA0, Sh::TILE_BYTES);
-    gdn_bulk_store(outp + Sh::TILE_BYTES, es, Sh::GATE_BYTES);
-    tma_store_commit();
-    tma_store_wait_read();  // shared memory stays valid until the copies have read it
-  }
 }
 
 // ---------------------------------------------------------------------------
