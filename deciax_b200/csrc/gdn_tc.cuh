@@ -120,7 +120,7 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
 constexpr int kGdnConvBlocks = 4;  // 64-token blocks per CTA of the conv pass
 
 template <int W>
-__global__ void __launch_bounds__(kGdnThreads) gdn_conv_bf16_kernel(GdnArgs a) {
+__global__ void __launch_bounds__(kGdnThreads, W <= 4 ? 3 : 1) gdn_conv_bf16_kernel(GdnArgs a) {
   using T = __nv_bfloat16;
   constexpr int C = kGdnChunk, DH = kGdnTcDim, VN = GdnVec<T>::N, GL = DH / VN, RPP = kGdnThreads / GL;
   constexpr int RT = C / RPP, NX = RT + W - 1;
@@ -143,16 +143,21 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_conv_bf16_kernel(GdnArgs a) {
   for (int blk = 0; blk < kGdnConvBlocks; ++blk) {
     const int t0 = (blockIdx.x * kGdnConvBlocks + blk) * C;  // uniform across the CTA
     if (t0 >= a.S) break;
-    float x[NX][VN];
+    uint32_t x[NX][VN / 2];  // the window's bf16 pairs, widened where used (exact)
 #pragma unroll
     for (int i = 0; i < NX; ++i) {
       const int tt = t0 + r0 - (W - 1) + i;
       const uint4 raw = (tt >= 0 && tt < a.S) ? *reinterpret_cast<const uint4*>(proj + (row0 + tt) * a.ldp + col)
                                               : make_uint4(0u, 0u, 0u, 0u);
-      const T* hv = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-      for (int c = 0; c < VN; ++c) x[i][c] = __bfloat162float(hv[c]);
+      x[i][0] = raw.x;
+      x[i][1] = raw.y;
+      x[i][2] = raw.z;
+      x[i][3] = raw.w;
     }
+    auto xv = [&](int i, int c) -> float {  // channel c of window row i
+      const uint32_t u = x[i][c >> 1];
+      return __uint_as_float((c & 1) ? (u & 0xFFFF0000u) : (u << 16));
+    };
 #pragma unroll
     for (int j = 0; j < RT; ++j) {
       const int t = t0 + r0 + j;
@@ -161,7 +166,7 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_conv_bf16_kernel(GdnArgs a) {
       for (int c = 0; c < VN; ++c) {
         float acc = 0.f;
 #pragma unroll
-        for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(x[j + i][c], w[c][i]));
+        for (int i = 0; i < W; ++i) acc = __fadd_rn(acc, __fmul_rn(xv(j + i, c), w[c][i]));
         y.v[c] = acc;
       }
       // bf16 roundings in pairs: z = T(acc), y = T(z sigmoid(z)) (text.py:31-39)
