@@ -67,6 +67,12 @@ CASES = [  # b, s, nh, nv, dh, width
     (1, 130, 2, 4, 128, 4),
     (3, 200, 1, 2, 128, 4),
     (1, 2048, 1, 2, 128, 4),  # 32 chunks of state recurrence (BF16: the tensor-core kernel)
+    # BF16 tensor-core passes: one value head per key head, four per key head, a lone token,
+    # an exact chunk, and a conv wider than four taps
+    (2, 1, 2, 2, 128, 4),
+    (2, 64, 2, 2, 128, 3),
+    (1, 100, 1, 4, 128, 2),
+    (1, 70, 1, 1, 128, 6),
 ]
 
 
