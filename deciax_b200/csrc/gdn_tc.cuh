@@ -60,6 +60,12 @@ __device__ __forceinline__ uint32_t gdn_sw_mn(int row, int col, int rows) {
                                ((col & 7) << 2));
 }
 
+// gdn_mn_half: a thread that updates row r of such a tile visits the two
+// 16-byte halves of each 32-byte chunk in the order given by bit 2 of r.  Rows
+// r and r + 4 put a column in the same chunk position under the swizzle, so a
+// warp of 32 consecutive rows then covers all 32 banks per float4 access (4
+// wavefronts instead of 8).
+
 // Shared-memory descriptor of such an MN-major tile: `lbo` bytes between
 // 32-column atoms, 512 bytes between 4-row K groups, layout type 1
 // (SWIZZLE_128B_BASE32B), descriptor version 1.
@@ -793,14 +799,21 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
           tmem_ld32(tmem + t_lane + Sh::D1 + j0, d);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4* p = reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e, C));
-            float4 u = *p;
-            u.x = to_tf32(fmaf(-ec, __uint_as_float(d[e]), u.x));
-            u.y = to_tf32(fmaf(-ec, __uint_as_float(d[e + 1]), u.y));
-            u.z = to_tf32(fmaf(-ec, __uint_as_float(d[e + 2]), u.z));
-            u.w = to_tf32(fmaf(-ec, __uint_as_float(d[e + 3]), u.w));
-            *p = u;
+          for (int e = 0; e < 32; e += 8) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const bool hi = (hh ^ ((c >> 2) & 1)) != 0;  // half order: gdn_mn_half
+              float x[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) x[k] = __uint_as_float(hi ? d[e + 4 + k] : d[e + k]);
+              float4* p = reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e + (hi ? 4 : 0), C));
+              float4 u = *p;
+              u.x = to_tf32(fmaf(-ec, x[0], u.x));
+              u.y = to_tf32(fmaf(-ec, x[1], u.y));
+              u.z = to_tf32(fmaf(-ec, x[2], u.z));
+              u.w = to_tf32(fmaf(-ec, x[3], u.w));
+              *p = u;
+            }
           }
         }
       }
@@ -834,10 +847,16 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
         tmem_ld32(tmem + t_lane + Sh::DV + j0, d);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e, C)) =
-              make_float4(to_tf32(__uint_as_float(d[e])), to_tf32(__uint_as_float(d[e + 1])),
-                          to_tf32(__uint_as_float(d[e + 2])), to_tf32(__uint_as_float(d[e + 3])));
+        for (int e = 0; e < 32; e += 8) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const bool hi = (hh ^ ((c >> 2) & 1)) != 0;  // half order: gdn_mn_half
+            float x[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[k] = to_tf32(__uint_as_float(hi ? d[e + 4 + k] : d[e + k]));
+            *reinterpret_cast<float4*>(sV + gdn_sw_mn(c, j0 + e + (hi ? 4 : 0), C)) = make_float4(x[0], x[1], x[2], x[3]);
+          }
+        }
       }
     }
     fence_async_smem();
@@ -899,14 +918,21 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       tmem_ld32(tmem + t_lane + Sh::D2 + j0, d);
       tmem_wait_ld();
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        float4* p = reinterpret_cast<float4*>(sS + gdn_sw_mn(lrow, j0 + e, DH));
-        float4 s = *p;
-        s.x = to_tf32(fmaf(s.x, decay, __uint_as_float(d[e])));
-        s.y = to_tf32(fmaf(s.y, decay, __uint_as_float(d[e + 1])));
-        s.z = to_tf32(fmaf(s.z, decay, __uint_as_float(d[e + 2])));
-        s.w = to_tf32(fmaf(s.w, decay, __uint_as_float(d[e + 3])));
-        *p = s;
+      for (int e = 0; e < 32; e += 8) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const bool hi = (hh ^ ((lrow >> 2) & 1)) != 0;  // half order: gdn_mn_half
+          float x[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) x[k] = __uint_as_float(hi ? d[e + 4 + k] : d[e + k]);
+          float4* p = reinterpret_cast<float4*>(sS + gdn_sw_mn(lrow, j0 + e + (hi ? 4 : 0), DH));
+          float4 s = *p;
+          s.x = to_tf32(fmaf(s.x, decay, x[0]));
+          s.y = to_tf32(fmaf(s.y, decay, x[1]));
+          s.z = to_tf32(fmaf(s.z, decay, x[2]));
+          s.w = to_tf32(fmaf(s.w, decay, x[3]));
+          *p = s;
+        }
       }
     }
     // ---- L: the next chunk's rows as operand tiles, q and k by lanes 0-63
