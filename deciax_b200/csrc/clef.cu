@@ -465,9 +465,12 @@ static void launch_gdn(Launcher& L, const GdnArgs& a, int dh) {
             done.insert(current_device());
           }
         }
-        REQUIRE(a.qkv_conv != nullptr && a.prep != nullptr && a.ldc >= static_cast<long long>(2 * a.nh + a.nv) * 128,
-                "the tensor-core Gated DeltaNet path needs its scratch (conv rows and prep records)");
-        REQUIRE(reinterpret_cast<uintptr_t>(a.prep) % 16 == 0, "prep records must be 16-byte aligned");
+        REQUIRE(a.qkv_conv != nullptr && a.prep != nullptr && a.a0_tiles != nullptr && a.v_tiles != nullptr &&
+                    a.ldc >= 2LL * a.nh * 128,
+                "the tensor-core Gated DeltaNet path needs its scratch (gdn_tc_bind_scratch)");
+        REQUIRE(reinterpret_cast<uintptr_t>(a.qkv_conv) % 16 == 0 && reinterpret_cast<uintptr_t>(a.prep) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(a.a0_tiles) % 16 == 0 && reinterpret_cast<uintptr_t>(a.v_tiles) % 16 == 0,
+                "Gated DeltaNet scratch must be 16-byte aligned");
         const int span = kGdnChunk * kGdnConvBlocks;
         const dim3 cgrid((a.S + span - 1) / span, 2 * a.nh + a.nv, a.B);
         if (a.width <= 4)
@@ -1651,11 +1654,7 @@ struct Model {
     a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(g_dh)));
     a.eps = cfg.rms_norm_eps;
     a.status = Lc.status;
-    if (gdn_conv_pass()) {
-      a.qkv_conv = ws.gconv.p;
-      a.ldc = static_cast<long long>(2 * g_nh_l + g_nv_l) * g_dh;
-      a.prep = static_cast<uint8_t*>(ws.gconv.p) + gdn_tc_conv_bytes(bt.b, bt.s, g_nh_l, g_nv_l);
-    }
+    if (gdn_conv_pass()) gdn_tc_bind_scratch(a, ws.gconv.p);
     Lc.cat = kCatGdn;
     launch_gdn<T>(Lc, a, g_dh);
     Lc.cat = kCatGemmO;
@@ -2531,18 +2530,18 @@ int clef_op_gdn_core(int dtype, const void* proj, int ldp, const void* conv, int
     a.qscale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(dh)));
     a.eps = eps;
     if (dtype == CLEF_DTYPE_BF16 && dh == 128) {
-      // the conv pass's rows, stream-ordered: allocated and freed on the caller's stream
-      a.ldc = static_cast<long long>(2 * nh + nv) * dh;
+      // the tensor-core passes' scratch, stream-ordered: allocated and freed on the caller's stream
+      void* scratch = nullptr;
       const size_t bytes = clef::gdn_tc_scratch_bytes(b, s, nh, nv);
-      CUDA_CHECK(cudaMallocFromPoolAsync(&a.qkv_conv, bytes, clef::op_scratch_pool(clef::current_device()), L.stream));
-      a.prep = static_cast<uint8_t*>(a.qkv_conv) + clef::gdn_tc_conv_bytes(b, s, nh, nv);
+      CUDA_CHECK(cudaMallocFromPoolAsync(&scratch, bytes, clef::op_scratch_pool(clef::current_device()), L.stream));
+      clef::gdn_tc_bind_scratch(a, scratch);
       try {
         clef::launch_gdn<bf16>(L, a, dh);
       } catch (...) {
-        cudaFreeAsync(a.qkv_conv, L.stream);
+        cudaFreeAsync(scratch, L.stream);
         throw;
       }
-      CUDA_CHECK(cudaFreeAsync(a.qkv_conv, L.stream));
+      CUDA_CHECK(cudaFreeAsync(scratch, L.stream));
     } else if (dtype == CLEF_DTYPE_BF16) {
       clef::launch_gdn<bf16>(L, a, dh);
     } else {

@@ -45,6 +45,10 @@ struct GdnArgs {
   long long ldc;
   // tensor-core path only: the prep pass's per-(chunk, value head, state) records
   void* prep;
+  // tensor-core path only: the conv pass's operand tiles for the chain pass, per
+  // (state, key head, chunk) [k; q dk^-1/2] and per (state, value head, chunk) v
+  void* a0_tiles;
+  void* v_tiles;
 };
 
 constexpr int kGdnChunk = 64;

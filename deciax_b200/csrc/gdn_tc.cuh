@@ -114,11 +114,13 @@ __device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, u
 }
 
 // Conv pass: causal conv + SiLU (text.py:31-39) of every q, k and v channel
-// and the L2 norms of q and k (reference.py:14-21), written as bf16 rows
-// [B*S, 2*nh*dh + nv*dh] (q heads, k heads, v heads, in projection column
-// order).  Every value is one the reference rounds to bf16, so the prep and
-// chain passes read exactly the values the CUDA-core kernel computes in
-// place; q leaves without the dk^-1/2 factor.  One CTA per (256-token span, q/k/v head, state): the
+// and the L2 norms of q and k (reference.py:14-21).  q and k leave as bf16
+// rows [B*S, 2*nh*dh] (q heads, k heads; q without the dk^-1/2 factor) for the
+// prep pass and as the chain's TF32 operand tiles [k; q dk^-1/2] per (state,
+// key head, chunk); v leaves as the chain's MN-major tile per (state, value
+// head, chunk).  Every value is one the reference rounds to bf16, so the prep
+// and chain passes read exactly the values the CUDA-core kernel computes in
+// place; rows past the sequence end are zero in the tiles.  One CTA per (256-token span, q/k/v head, state): the
 // q and k heads are computed once, not once per value head that shares them,
 // and the pass runs at full occupancy (each CTA walks kGdnConvBlocks blocks
 // with its taps in registers).  The sliding-window arithmetic is
@@ -139,7 +141,7 @@ __global__ void __launch_bounds__(kGdnThreads, W <= 4 ? 3 : 1) gdn_conv_bf16_ker
   const T* convw = static_cast<const T*>(a.conv);
   T* dst = static_cast<T*>(a.qkv_conv);
   const long long row0 = static_cast<long long>(b) * a.S;
-  const int shift = W - a.width;
+  const int shift = W - a.width, chunks = (a.S + C - 1) / C;
   float w[VN][W];  // this thread's taps, loaded once for all its blocks
 #pragma unroll
   for (int c = 0; c < VN; ++c)
@@ -195,7 +197,29 @@ __global__ void __launch_bounds__(kGdnThreads, W <= 4 ? 3 : 1) gdn_conv_bf16_ker
           round2_bf16(y.v[c], y.v[c + 1]);
         }
       }
-      if (t < a.S) y.store(dst + (row0 + t) * a.ldc + kh * DH + g * VN);
+      const int rr = r0 + j, ci = t0 / C;
+      if (kind < 2) {
+        if (t < a.S) y.store(dst + (row0 + t) * a.ldc + kh * DH + g * VN);
+        // the chain's operand tile: k -> rows 0-63, q x dk^-1/2 (TF32) -> rows 64-127
+        const int hk = kind == 0 ? kh : kh - a.nh;
+        uint8_t* tile = static_cast<uint8_t*>(a.a0_tiles) +
+                        ((static_cast<long long>(b) * a.nh + hk) * chunks + ci) * static_cast<long long>(2 * C * DH * 4);
+        float o[VN];
+#pragma unroll
+        for (int c = 0; c < VN; ++c) o[c] = kind == 0 ? to_tf32(y.v[c] * a.qscale) : y.v[c];
+        const int row = kind == 1 ? rr : C + rr;
+#pragma unroll
+        for (int c = 0; c < VN; c += 4)
+          *reinterpret_cast<float4*>(tile + gdn_sw(row, g * VN + c, 2 * C)) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+      } else {
+        // the chain's v tile (MN-major: token rows, value-dim columns)
+        uint8_t* tile = static_cast<uint8_t*>(a.v_tiles) +
+                        ((static_cast<long long>(b) * a.nv + (kh - 2 * a.nh)) * chunks + ci) * static_cast<long long>(C * DH * 4);
+#pragma unroll
+        for (int c = 0; c < VN; c += 4)
+          *reinterpret_cast<float4*>(tile + gdn_sw_mn(rr, g * VN + c, C)) =
+              make_float4(y.v[c], y.v[c + 1], y.v[c + 2], y.v[c + 3]);
+      }
     }
   }
 }
@@ -557,16 +581,38 @@ struct GdnChainShape {
                 "bulk copies move 16-byte multiples from 16-byte aligned records");
 };
 
-// Scratch of the tensor-core path for B states of S tokens: the conv pass's
-// bf16 rows [B*S, (2 nh + nv) 128], then (256-byte aligned) the prep pass's
-// records, one of GdnPrepShape::OUT_BYTES per (state, value head, chunk).
-inline size_t gdn_tc_conv_bytes(int B, int S, int nh, int nv) {
-  const size_t bytes = static_cast<size_t>(B) * S * (2 * nh + nv) * kGdnTcDim * 2;
-  return (bytes + 255) & ~size_t(255);
-}
-inline size_t gdn_tc_scratch_bytes(int B, int S, int nh, int nv) {
+// Scratch of the tensor-core path for B states of S tokens, in order, each part
+// 256-byte aligned: the conv pass's bf16 q/k rows [B*S, 2 nh 128] (q heads, k
+// heads), the chain's [k; q dk^-1/2] operand tiles (GdnChainShape::A0_BYTES per
+// state, key head and chunk), its v tiles (V_BYTES per state, value head and
+// chunk), and the prep pass's records (GdnPrepShape::OUT_BYTES per state, value
+// head and chunk).
+struct GdnTcScratch {
+  size_t rows = 0, a0 = 0, v = 0, prep = 0, total = 0;
+  GdnTcScratch(int B, int S, int nh, int nv);
+};
+
+inline GdnTcScratch::GdnTcScratch(int B, int S, int nh, int nv) {
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   const size_t chunks = (static_cast<size_t>(S) + kGdnChunk - 1) / kGdnChunk;
-  return gdn_tc_conv_bytes(B, S, nh, nv) + static_cast<size_t>(B) * nv * chunks * GdnPrepShape::OUT_BYTES;
+  rows = 0;
+  a0 = up(static_cast<size_t>(B) * S * 2 * nh * kGdnTcDim * 2);
+  v = a0 + up(static_cast<size_t>(B) * nh * chunks * GdnChainShape::A0_BYTES);
+  prep = v + up(static_cast<size_t>(B) * nv * chunks * GdnChainShape::V_BYTES);
+  total = prep + static_cast<size_t>(B) * nv * chunks * GdnPrepShape::OUT_BYTES;
+}
+
+inline size_t gdn_tc_scratch_bytes(int B, int S, int nh, int nv) { return GdnTcScratch(B, S, nh, nv).total; }
+
+// Point a's tensor-core buffers into `base` (gdn_tc_scratch_bytes(a.B, a.S, a.nh, a.nv) bytes).
+inline void gdn_tc_bind_scratch(GdnArgs& a, void* base) {
+  const GdnTcScratch sc(a.B, a.S, a.nh, a.nv);
+  uint8_t* p = static_cast<uint8_t*>(base);
+  a.qkv_conv = p + sc.rows;
+  a.ldc = 2LL * a.nh * kGdnTcDim;
+  a.a0_tiles = p + sc.a0;
+  a.v_tiles = p + sc.v;
+  a.prep = p + sc.prep;
 }
 
 // Untiled bulk copy global -> this CTA's shared memory, completing on `bar`
@@ -578,71 +624,26 @@ __device__ __forceinline__ void gdn_bulk_load(void* dst, const void* src, uint32
                : "memory");
 }
 
-// Stage the q, k, v rows [t0, t0 + C) of the conv pass (bf16) as TF32
-// operand tiles: k -> A0 rows 0-63, q x dk^-1/2 -> A0 rows 64-127 (K-major),
-// v -> V (MN-major).  NTHR threads (lt = 0 .. NTHR-1), 16 per row and 8
-// channels each; rows past the sequence end are zero.
-template <int NTHR, int K0, int K1>  // kinds [K0, K1) of q = 0, k = 1, v = 2
-__device__ __forceinline__ void gdn_stage_rows(uint8_t* sA0, uint8_t* sV, const __nv_bfloat16* rows, int valid,
-                                               long long ldc, int q_col, int k_col, int v_col, float qscale, int lt) {
-  using T = __nv_bfloat16;
-  constexpr int C = kGdnChunk, RS = NTHR / 16, PASSES = 4;  // rows per pass; passes per batch of loads
-  static_assert(C % (RS * PASSES) == 0 && 0 <= K0 && K0 < K1 && K1 <= 3, "row batches, kinds");
-  const int g8 = (lt % 16) * 8;
-#pragma unroll
-  for (int r0 = 0; r0 < C; r0 += RS * PASSES) {
-    uint4 raw[3][PASSES];
-#pragma unroll
-    for (int i = 0; i < PASSES; ++i) {
-      const int r = r0 + lt / 16 + RS * i;
-      const T* src = rows + r * ldc + g8;
-#pragma unroll
-      for (int kind = K0; kind < K1; ++kind)
-        raw[kind][i] = r < valid ? *reinterpret_cast<const uint4*>(src + (kind == 0 ? q_col : kind == 1 ? k_col : v_col))
-                                 : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < PASSES; ++i) {
-      const int r = r0 + lt / 16 + RS * i;
-#pragma unroll
-      for (int kind = K0; kind < K1; ++kind) {
-        const T* hv = reinterpret_cast<const T*>(&raw[kind][i]);
-        float y[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) y[c] = kind == 0 ? to_tf32(__bfloat162float(hv[c]) * qscale) : __bfloat162float(hv[c]);
-#pragma unroll
-        for (int c = 0; c < 8; c += 4) {
-          const float4 v4 = make_float4(y[c], y[c + 1], y[c + 2], y[c + 3]);
-          if (kind == 2)
-            *reinterpret_cast<float4*>(sV + gdn_sw_mn(r, g8 + c, C)) = v4;
-          else
-            *reinterpret_cast<float4*>(sA0 + gdn_sw(kind == 0 ? C + r : r, g8 + c, 2 * C)) = v4;
-        }
-      }
-    }
-  }
-}
-
 // Output row staging over the (read) operand tile: row c, columns j, 128
 // floats per row with 16-byte chunks XOR-permuted by c % 32 (a warp's 32 rows
 // at one column fall in distinct chunks).
 __device__ __forceinline__ int gdn_ob(int c, int j) { return c * 128 + (((j >> 2) ^ (c & 31)) << 2) + (j & 3); }
 
 // One CTA per (value head, state) walks the chunks with the FP32 state S in
-// shared memory.  Per chunk: the prep pass's gates and tile [T diag(beta); M]
-// arrive by bulk copy (the gates while the previous chunk finishes, the tile
-// once its output rows are read); q, k, v were staged as TF32 operand tiles
-// during the previous chunk's output phase (A0 = [k; q dk^-1/2], V);
+// shared memory.  Per chunk, everything it reads arrives by bulk copy while
+// the previous chunk finishes: the conv pass's TF32 operand tiles A0 = [k; q
+// dk^-1/2] (once the previous chunk's K~^T has read A0) and V (once its last
+// products have read V), the prep pass's gates (with V) and its tile
+// [T diag(beta); M] (once the previous chunk's output rows are read);
 //   M1 D1 = A0 S (rows 0-63 k S, rows 64-127 q S);
 //   P  K~^T = (k e^{g_C - g})^T into tensor memory; R = v - e^g (k S) in place of v;
 //   MV D_V = [T diag(beta); M] R: rows 0-63 V_new, stored in place of R;
 //   M3 D_V = [T diag(beta); M] V_new: rows 64-127 M V_new; M4 D2 = K~^T V_new;
 //   O  lanes 64-127 (warps 2, 3, 6, 7): rows e^g (q S) + M V_new
 //      (reference.py:85) over the tile, S = S e^{g_C} + D2 (reference.py:86)
-//      on their lanes, the next chunk's v tile; lanes 0-63 (warps 0, 1, 4,
-//      5): the state update on theirs, the next chunk's q and k tiles; then
-//      the next chunk's M1 is issued and all warps apply the gated RMSNorm x
-//      SiLU(z) (text.py:61-67) while it runs.
+//      on their lanes; lanes 0-63 (warps 0, 1, 4, 5): the state update on
+//      theirs; then the next chunk's M1 is issued and all warps apply the
+//      gated RMSNorm x SiLU(z) (text.py:61-67) while it runs.
 // Tensor memory: D1 [0, 128), D_V [128, 256), D2 [256, 384), K~^T [384, 448).
 __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   using Sh = GdnChainShape;
@@ -664,7 +665,9 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(nws + DH);
   uint64_t* tile_bar = mma_bar + 1;
   uint64_t* gate_bar = tile_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gate_bar + 1);
+  uint64_t* a0_bar = gate_bar + 1;
+  uint64_t* v_bar = a0_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_bar + 1);
   static_assert(C * 128 * 4 <= Sh::T_BYTES, "output rows over the tile");
 
   const int h = blockIdx.x, b = blockIdx.y;
@@ -675,11 +678,14 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   const int hk = h / (a.nv / a.nh);
   const T* proj = static_cast<const T*>(a.proj);
   const T* nw = static_cast<const T*>(a.norm_w);
-  const T* qkv = static_cast<const T*>(a.qkv_conv);
   T* out = static_cast<T*>(a.out);
   const long long row0 = static_cast<long long>(b) * a.S;
-  const int q_col = hk * DH, k_col = (a.nh + hk) * DH, v_col = (2 * a.nh + h) * DH;  // columns of the conv pass
   const int chunks = (a.S + C - 1) / C;
+  // the conv pass's operand tiles of this CTA's key head and value head, chunk 0
+  const uint8_t* a0_src = static_cast<const uint8_t*>(a.a0_tiles) +
+                          (static_cast<long long>(b) * a.nh + hk) * chunks * static_cast<long long>(Sh::A0_BYTES);
+  const uint8_t* v_src = static_cast<const uint8_t*>(a.v_tiles) +
+                         (static_cast<long long>(b) * a.nv + h) * chunks * static_cast<long long>(Sh::V_BYTES);
   const uint8_t* prep = static_cast<const uint8_t*>(a.prep) +
                         (static_cast<long long>(b) * a.nv + h) * chunks * static_cast<long long>(GdnPrepShape::OUT_BYTES);
 
@@ -687,6 +693,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     mbar_init(mma_bar, 1);
     mbar_init(tile_bar, 1);
     mbar_init(gate_bar, 1);
+    mbar_init(a0_bar, 1);
+    mbar_init(v_bar, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -695,14 +703,12 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   }
   for (int i = tid; i < DH * DH; i += kGdnThreads) reinterpret_cast<float*>(sS)[i] = 0.f;  // S = 0 (any layout)
   if (tid < DH) nws[tid] = to_f32(nw[tid]);
-  gdn_stage_rows<kGdnThreads, 0, 3>(sA0, sV, qkv + row0 * a.ldc, a.S, a.ldc, q_col, k_col, v_col, a.qscale, tid);
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  uint32_t mma_phase = 0, tile_phase = 0, gate_phase = 0;
-  bool tile_pending = false, gate_pending = false;  // thread 0: a copy is in flight
+  uint32_t mma_phase = 0, tile_phase = 0, gate_phase = 0, a0_phase = 0, v_phase = 0;
+  bool tile_pending = false, gate_pending = false, a0_pending = false, v_pending = false;  // thread 0: copies in flight
   // chunk ci's record: the tile into sT, the gates into gates[ci & 1]
   auto load_tile = [&](int ci) {
     mbar_arrive_expect_tx(tile_bar, GdnPrepShape::TILE_BYTES);
@@ -716,7 +722,20 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
                   GdnPrepShape::GATE_BYTES, gate_bar);
     gate_pending = true;
   };
+  // chunk ci's operand tiles: [k; q dk^-1/2] into A0, v into V
+  auto load_a0 = [&](int ci) {
+    mbar_arrive_expect_tx(a0_bar, Sh::A0_BYTES);
+    gdn_bulk_load(sA0, a0_src + static_cast<long long>(ci) * Sh::A0_BYTES, Sh::A0_BYTES, a0_bar);
+    a0_pending = true;
+  };
+  auto load_v = [&](int ci) {
+    mbar_arrive_expect_tx(v_bar, Sh::V_BYTES);
+    gdn_bulk_load(sV, v_src + static_cast<long long>(ci) * Sh::V_BYTES, Sh::V_BYTES, v_bar);
+    v_pending = true;
+  };
   if (tid == 0) {
+    load_a0(0);
+    load_v(0);
     load_gates(0);
     load_tile(0);
   }
@@ -740,7 +759,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
 
   const uint32_t a0 = smem_u32(sA0), sv = smem_u32(sV), st = smem_u32(sT), ss_addr = smem_u32(sS);
   // ---- M1: D1 = [k; q] S (the k operand values are exact in TF32: bf16 after
-  // the norm), issued as soon as a chunk's rows are staged and S is updated ----
+  // the norm), issued as soon as a chunk's A0 tile has landed and S is updated ----
   auto issue_m1 = [&]() {
 #pragma unroll
     for (int kk = 0; kk < DH / 8; ++kk) {
@@ -750,35 +769,30 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     }
     umma_commit(mma_bar);
   };
-  if (tid == 32) issue_m1();
+  if (tid == 32 && mbar_wait(a0_bar, a0_phase, a.status, kTimeoutMma)) issue_m1();
   for (int ci = 0; ci < chunks; ++ci) {
     const int t0 = ci * C;
     const float* es = gates + (ci & 1) * 2 * C;  // e^g
     const float* ws = es + C;                    // e^(g_last - g)
     // the chunk's z rows for the gated norm (16 threads per 256-byte row), and
-    // the next chunk's rows head for L2 (64 rows x 4 segments of 256 bytes),
-    // while M1 runs
+    // the next chunk's z rows head for L2, while M1 runs
 #pragma unroll
     for (int i = 0; i < C * 16 / kGdnThreads; ++i) {
       const int idx = tid + kGdnThreads * i, c = idx >> 4, e8 = (idx & 15) * 8, t = t0 + c;
       cp_async16(zs + c * Sh::ZLD + e8, proj + (row0 + (t < a.S ? t : 0)) * a.ldp + a.z_col + h * DH + e8, t < a.S);
     }
     cp_async_commit();
-    {
-      const int r = tid >> 2, seg = tid & 3, t = t0 + C + r;
-      if (t < a.S) {
-        const T* src = seg < 3 ? qkv + (row0 + t) * a.ldc + (seg == 0 ? q_col : seg == 1 ? k_col : v_col)
-                               : proj + (row0 + t) * a.ldp + a.z_col + h * DH;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(src + 64));
-      }
-    }
+    if (tid < 2 * C && t0 + C + (tid >> 1) < a.S)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(proj + (row0 + t0 + C + (tid >> 1)) * a.ldp + a.z_col + h * DH +
+                                                      64 * (tid & 1)));
     {
       const bool gate_ok = copy_wait(gate_bar, gate_phase, gate_pending);
+      const bool a0_ok = copy_wait(a0_bar, a0_phase, a0_pending);
+      const bool v_ok = copy_wait(v_bar, v_phase, v_pending);
       const bool mma_ok = mbar_wait(mma_bar, mma_phase, a.status, kTimeoutMma);
       mma_phase ^= 1;
       tc_fence_after();
-      if (!__syncthreads_and(gate_ok && mma_ok)) break;
+      if (!__syncthreads_and(gate_ok && a0_ok && v_ok && mma_ok)) break;
     }
     // ---- P: K~^T (lane = key dim, columns c in [32 half, +32)) and R = v - e^g (k S)
     // (lanes 0-63, value dims [64 half, +64)) ----
@@ -825,6 +839,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       const bool tile_ok = copy_wait(tile_bar, tile_phase, tile_pending);
       if (!__syncthreads_and(tile_ok)) break;
     }
+    // A0 is read (M1, K~^T): the next chunk's [k; q] tile comes in
+    if (tid == 0 && ci + 1 < chunks) load_a0(ci + 1);
     // ---- MV: D_V = [T diag(beta); M] R (lanes 0-63: V_new; lanes 64-127 unused) ----
     if (tid == 32) {
       tc_fence_after();
@@ -875,9 +891,12 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
       umma_commit(mma_bar);
     }
     if (!mma_wait()) break;
-    // every operand tile is read: the next chunk's gates come in now, its tile
-    // once the output rows (over the tile) are read
-    if (tid == 0 && ci + 1 < chunks) load_gates(ci + 1);
+    // every operand tile is read: the next chunk's gates and v tile come in now,
+    // its record tile once the output rows (over the tile) are read
+    if (tid == 0 && ci + 1 < chunks) {
+      load_gates(ci + 1);
+      load_v(ci + 1);
+    }
     const float decay = es[C - 1];
     if (lrow >= C) {
       // ---- O1 (lanes 64-127): o = T(e^g (q S) + M V_new) into the output
@@ -935,22 +954,13 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
         }
       }
     }
-    // ---- L: the next chunk's rows as operand tiles, q and k by lanes 0-63
-    // (while the others finish the output rows), v by lanes 64-127 ----
-    if (ci + 1 < chunks) {
-      const T* rows = qkv + (row0 + t0 + C) * a.ldc;
-      const int lt = (warp >> 2) * 64 + (quarter & 1) * 32 + lane;
-      if (lrow < C)
-        gdn_stage_rows<kGdnThreads / 2, 0, 2>(sA0, sV, rows, a.S - t0 - C, a.ldc, q_col, k_col, v_col, a.qscale, lt);
-      else
-        gdn_stage_rows<kGdnThreads / 2, 2, 3>(sA0, sV, rows, a.S - t0 - C, a.ldc, q_col, k_col, v_col, a.qscale, lt);
-    }
     cp_async_wait<0>();  // this thread's z copies, read by others after the barrier
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid == 32 && ci + 1 < chunks) issue_m1();  // overlaps the gated norm below
+    if (tid == 32 && ci + 1 < chunks && mbar_wait(a0_bar, a0_phase, a.status, kTimeoutMma))
+      issue_m1();  // overlaps the gated norm below
     // ---- O2 (all threads, one row per lane, 32 columns per warp quarter of
     // the CTA): gated RMSNorm x SiLU(z) (text.py:61-67) ----
     {
@@ -989,6 +999,8 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
   // memory is released (bounded: the status is already set)
   if (tid == 0 && tile_pending) mbar_wait(tile_bar, tile_phase, a.status, kTimeoutMma);
   if (tid == 0 && gate_pending) mbar_wait(gate_bar, gate_phase, a.status, kTimeoutMma);
+  if (tid == 0 && a0_pending) mbar_wait(a0_bar, a0_phase, a.status, kTimeoutMma);
+  if (tid == 0 && v_pending) mbar_wait(v_bar, v_phase, a.status, kTimeoutMma);
   cp_async_wait<0>();  // and this thread's z copies
   tc_fence_before();
   __syncthreads();
