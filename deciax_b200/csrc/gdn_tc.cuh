@@ -961,30 +961,30 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     tc_fence_after();
     if (tid == 32 && ci + 1 < chunks && mbar_wait(a0_bar, a0_phase, a.status, kTimeoutMma))
       issue_m1();  // overlaps the gated norm below
-    // ---- O2 (all threads, one row per lane, 32 columns per warp quarter of
-    // the CTA): gated RMSNorm x SiLU(z) (text.py:61-67) ----
+    // ---- O2 (all threads; 16 per row, 8 columns each, so that a warp's
+    // loads and stores cover two whole rows): gated RMSNorm x SiLU(z)
+    // (text.py:61-67) ----
     {
-      const int c = tid & (C - 1), q32 = (tid >> 6) * 32, t = t0 + c;
-      if (t < a.S) {
-        const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
-        const T* zrow = zs + c * Sh::ZLD + q32;
-        T* orow = out + (row0 + t) * a.ldo + h * DH + q32;
+      const int col = (tid & 15) * 8;
 #pragma unroll
-        for (int e8 = 0; e8 < 32; e8 += 8) {
+      for (int pass = 0; pass < C * 16 / kGdnThreads; ++pass) {
+        const int c = pass * (kGdnThreads / 16) + (tid >> 4), t = t0 + c;
+        if (t < a.S) {
+          const float rs = rsqrtf((red[c] + red[C + c]) / DH + a.eps);
           GdnVec<T> z, res;
-          z.load(zrow + e8);
-          const float4 o0 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, q32 + e8));
-          const float4 o1 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, q32 + e8 + 4));
+          z.load(zs + c * Sh::ZLD + col);
+          const float4 o0 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, col));
+          const float4 o1 = *reinterpret_cast<const float4*>(ob + gdn_ob(c, col + 4));
           float n[8] = {o0.x * rs, o0.y * rs, o0.z * rs, o0.w * rs, o1.x * rs, o1.y * rs, o1.z * rs, o1.w * rs};
 #pragma unroll
           for (int e = 0; e < 8; e += 2) round2_bf16(n[e], n[e + 1]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) n[e] *= nws[q32 + e8 + e];
+          for (int e = 0; e < 8; ++e) n[e] *= nws[col + e];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) round2_bf16(n[e], n[e + 1]);
 #pragma unroll
           for (int e = 0; e < 8; ++e) res.v[e] = n[e] * (z.v[e] * sigmoid_fast(z.v[e]));
-          res.store(orow + e8);
+          res.store(out + (row0 + t) * a.ldo + h * DH + col);
         }
       }
     }
