@@ -636,7 +636,8 @@ __device__ __forceinline__ int gdn_ob(int c, int j) { return c * 128 + (((j >> 2
 // products have read V), the prep pass's gates (with V) and its tile
 // [T diag(beta); M] (once the previous chunk's output rows are read);
 //   M1 D1 = A0 S (rows 0-63 k S, rows 64-127 q S);
-//   P  K~^T = (k e^{g_C - g})^T into tensor memory; R = v - e^g (k S) in place of v;
+//   P  K~^T = (k e^{g_C - g})^T into tensor memory (lanes 0-63: during the previous
+//      chunk's output phase); R = v - e^g (k S) in place of v;
 //   MV D_V = [T diag(beta); M] R: rows 0-63 V_new, stored in place of R;
 //   M3 D_V = [T diag(beta); M] V_new: rows 64-127 M V_new; M4 D2 = K~^T V_new;
 //   O  lanes 64-127 (warps 2, 3, 6, 7): rows e^g (q S) + M V_new
@@ -798,12 +799,14 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     // (lanes 0-63, value dims [64 half, +64)) ----
     {
       uint32_t d[32];
+      if (lrow >= C || ci == 0) {  // lanes 0-63 of later chunks: written during the previous chunk
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int c = 32 * half + e;
-        d[e] = __float_as_uint(to_tf32(*reinterpret_cast<const float*>(sA0 + gdn_sw(c, lrow, 2 * C)) * ws[c]));
+        for (int e = 0; e < 32; ++e) {
+          const int c = 32 * half + e;
+          d[e] = __float_as_uint(to_tf32(*reinterpret_cast<const float*>(sA0 + gdn_sw(c, lrow, 2 * C)) * ws[c]));
+        }
+        tmem_st32(tmem + t_lane + Sh::KT + 32 * half, d);
       }
-      tmem_st32(tmem + t_lane + Sh::KT + 32 * half, d);
       if (lrow < C) {
         const int c = lrow;
         const float ec = es[c];
@@ -953,6 +956,21 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
           *p = s;
         }
       }
+    }
+    // ---- the next chunk's K~^T on lanes 0-63, while warps 2, 3, 6, 7 finish the
+    // output rows (its A0 tile and gates have arrived by now; a failed wait
+    // leaves it to the loop head's waits, which then end the walk) ----
+    if (lrow < C && ci + 1 < chunks && mbar_wait(a0_bar, a0_phase, a.status, kTimeoutMma) &&
+        mbar_wait(gate_bar, gate_phase, a.status, kTimeoutMma)) {
+      const float* wsn = gates + ((ci + 1) & 1) * 2 * C + C;
+      uint32_t d[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int c = 32 * half + e;
+        d[e] = __float_as_uint(to_tf32(*reinterpret_cast<const float*>(sA0 + gdn_sw(c, lrow, 2 * C)) * wsn[c]));
+      }
+      tmem_st32(tmem + t_lane + Sh::KT + 32 * half, d);
+      tmem_wait_st();
     }
     cp_async_wait<0>();  // this thread's z copies, read by others after the barrier
     fence_async_smem();
