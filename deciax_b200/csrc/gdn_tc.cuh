@@ -984,6 +984,9 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
     // (text.py:61-67) ----
     {
       const int col = (tid & 15) * 8;
+      float wn[8];  // this thread's columns of the norm weight
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wn[e] = nws[col + e];
 #pragma unroll
       for (int pass = 0; pass < C * 16 / kGdnThreads; ++pass) {
         const int c = pass * (kGdnThreads / 16) + (tid >> 4), t = t0 + c;
@@ -997,7 +1000,7 @@ __global__ void __launch_bounds__(kGdnThreads, 1) gdn_chain_kernel(GdnArgs a) {
 #pragma unroll
           for (int e = 0; e < 8; e += 2) round2_bf16(n[e], n[e + 1]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) n[e] *= nws[col + e];
+          for (int e = 0; e < 8; ++e) n[e] *= wn[e];
 #pragma unroll
           for (int e = 0; e < 8; e += 2) round2_bf16(n[e], n[e + 1]);
 #pragma unroll
