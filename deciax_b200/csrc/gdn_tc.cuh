@@ -574,7 +574,7 @@ struct GdnChainShape {
   static constexpr int ZLD = DH + 8;                      // z rows: bf16, 272-byte rows
   static constexpr uint32_t Z_BYTES = C * ZLD * 2;
   static constexpr uint32_t MISC_FLOATS = 2 * C + DH;     // output-row sums of squares, norm weight
-  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + G_BYTES + Z_BYTES + MISC_FLOATS * 4 + 64;  // + 3 mbarriers, TMEM slot
+  static constexpr size_t SMEM = 1024 + S_BYTES + A0_BYTES + V_BYTES + T_BYTES + G_BYTES + Z_BYTES + MISC_FLOATS * 4 + 64;  // + 5 mbarriers, TMEM slot
   static constexpr uint32_t D1 = 0, DV = 128, D2 = 256, KT = 384, TMEM_COLS = 512;
   static_assert(GdnPrepShape::TILE_BYTES % 16 == 0 && GdnPrepShape::GATE_BYTES % 16 == 0 &&
                     GdnPrepShape::OUT_BYTES % 16 == 0,
