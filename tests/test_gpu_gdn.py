@@ -3,10 +3,10 @@
 * ``clef_op_gdn_core`` (conv + SiLU, L2 norms, gates, chunked delta rule,
   gated RMSNorm x SiLU(z)) against ``delta_net_core`` of the oracle
   (models/qwen3_5/text.py:48-67, kernels/gdn/reference.py:40-92) at every
-  supported head dim, key/value head ratios 1-3, lengths around the 64-token
-  chunk (1, 63, 64, 65, 130) and up to 2048, and conv widths 1-4 (BF16 at
-  head dim 128 runs the tensor-core kernel, every other case the CUDA-core
-  one);
+  supported head dim, key/value head ratios 1-4, lengths around the 64-token
+  chunk (1, 63, 64, 65, 70, 100, 130) and up to 2048, and conv widths 1-6
+  (BF16 at head dim 128 runs the tensor-core conv, prep and chain passes,
+  every other case the CUDA-core kernel);
 * whole models with GDN layers: the Transformers ``Qwen3_5TextModel`` fixture
   of the reference test (tests/test_qwen3_5.py:43-87: 3 GDN + 1 full layer)
   through the CUDA FP32 path, and synthetic mixed stacks against the oracle in
@@ -66,7 +66,7 @@ CASES = [  # b, s, nh, nv, dh, width
     (2, 65, 1, 3, 64, 1),
     (1, 130, 2, 4, 128, 4),
     (3, 200, 1, 2, 128, 4),
-    (1, 2048, 1, 2, 128, 4),  # 32 chunks of state recurrence (BF16: the tensor-core kernel)
+    (1, 2048, 1, 2, 128, 4),  # 32 chunks of state recurrence (BF16: the tensor-core passes)
     # BF16 tensor-core passes: one value head per key head, four per key head, a lone token,
     # an exact chunk, and a conv wider than four taps
     (2, 1, 2, 2, 128, 4),
